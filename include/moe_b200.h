@@ -1,0 +1,165 @@
+/*
+ * moe_b200.h — C ABI of the B200-native MoEInfra quantized-expert hot path.
+ *
+ * Conventions (every entry point):
+ *   - plain pointers and sizes; no torch or C++ types cross this boundary;
+ *   - every device pointer is owned by the caller; the library never allocates
+ *     device memory (scratch comes from a caller-provided workspace whose size
+ *     the *_workspace_size functions report);
+ *   - all work is enqueued on the caller's stream (`stream` is a cudaStream_t
+ *     passed as void*; NULL means the legacy default stream);
+ *   - the return value is a moe_status_t; nothing throws across the ABI;
+ *     moe_status_string() turns it into text.
+ *
+ * Numeric formats follow the reference's NF4 expert store (per projection:
+ * packed weight uint8 [out*in/2], element 2j in the HIGH nibble of byte j,
+ * row-major over [out, in]; fp32 absmax [out*in/64]; fp32 codebook [16]).
+ * fp16 and bf16 values are passed as uint16_t bit patterns.
+ *
+ * File:line citations refer to the reference project ParshwaPatel-07/MoEInfra.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum moe_status {
+  MOE_OK = 0,
+  MOE_ERR_INVALID_ARG = 1,
+  MOE_ERR_UNSUPPORTED = 2,
+  MOE_ERR_CUDA = 3,
+  MOE_ERR_WORKSPACE = 4,
+  MOE_ERR_ALIGNMENT = 5,
+  MOE_ERR_TIMEOUT = 6
+} moe_status_t;
+
+#define MOE_MAX_EXPERTS 16
+#define MOE_NF4_BLOCKSIZE 64
+
+/* One NF4-quantized linear layer [rows=out, cols=in] in store layout. */
+typedef struct moe_nf4_matrix {
+  const uint8_t* q;     /* packed codes, rows*cols/2 bytes, 16-byte aligned */
+  const float* absmax;  /* fp32, rows*cols/64 (already de-nested)          */
+  const float* code;    /* fp32[16] codebook (the store's quant_map)        */
+} moe_nf4_matrix_t;
+
+/* One Mixtral SwiGLU expert: w1, w3 are [inter, hidden]; w2 is [hidden, inter]. */
+typedef struct moe_nf4_expert {
+  moe_nf4_matrix_t w1;
+  moe_nf4_matrix_t w3;
+  moe_nf4_matrix_t w2;
+} moe_nf4_expert_t;
+
+/* Text for a status code (static storage). */
+const char* moe_status_string(int status);
+
+/* Library build identifier (static storage). */
+const char* moe_version(void);
+
+/* ---------------------------------------------------------------------------
+ * NF4 blockwise dequant to bf16, bit-exact:
+ *   out[i] = bf16_rn(code[nib(i)] * absmax[i / blocksize])   (fp32 product)
+ * Replaces bitsandbytes dequantize_4bit as reached from
+ * transfer/nf4_reconstruct.py:45-54 (QuantState, dtype bf16 at :12).
+ * numel must be even; blocksize a power of two >= 32.
+ */
+int moe_nf4_dequant(const uint8_t* q, const float* absmax, const float* code,
+                    int64_t numel, int blocksize, uint16_t* out_bf16,
+                    void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Rebuild fp32 absmax from its double quantization (nested QuantState,
+ * transfer/nf4_reconstruct.py:17-38, blocksize 256 at :13):
+ *   out[b] = fp32(fp32(code2[qabs[b]] * absmax2[b / blocksize2]) + offset)
+ */
+int moe_nf4_nested_absmax(const uint8_t* qabs, const float* absmax2,
+                          const float* code2, float offset, int64_t nblocks,
+                          int blocksize2, float* out_absmax, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused top-k router: logits = fp16(h . Wg^T) (fp32 accumulation), fp32
+ * softmax over E, top-k, renormalised over the k chosen.
+ * Replaces ExpertRouter.logits/route_with_logits (engine/router.py:50-94).
+ *   h      fp16 [T, H]      wg   fp16 [E, H]
+ *   logits fp16 [T, E] (may be NULL)
+ *   weights fp32 [T, k]     indices int64 [T, k] (descending probability;
+ *   exact ties resolved toward the lower expert index)
+ * Limits: 1 <= E <= 32, 1 <= k <= E, H % 8 == 0.
+ */
+int moe_router_topk(const uint16_t* h, const uint16_t* wg, int64_t T, int H,
+                    int E, int k, uint16_t* logits, float* weights,
+                    int64_t* indices, void* stream);
+
+/* Softmax/top-k/renormalise stage alone, from fp16 logits [T, E]
+ * (engine/router.py:81-92). */
+int moe_router_topk_from_logits(const uint16_t* logits, int64_t T, int E,
+                                int k, float* weights, int64_t* indices,
+                                void* stream);
+
+/* ---------------------------------------------------------------------------
+ * SwiGLU expert on n fp16 tokens: y = w2(silu(w1 x) * w3 x)
+ * Replaces ReconstructedNF4Expert.forward (transfer/nf4_reconstruct.py:152-155)
+ * with the bitsandbytes Linear4bit path it reaches: n == 1 uses the 4-bit
+ * GEMV semantics (fp16(fp16(code)*fp16(absmax)) weights), n > 1 the
+ * dequant-to-bf16-then-fp16-GEMM semantics.
+ *   x fp16 [n, hidden]  ->  y fp16 [n, hidden]
+ * Requires hidden % 128 == 0 and inter % 128 == 0.
+ */
+size_t moe_expert_workspace_size(int64_t n, int hidden, int inter);
+int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t* x,
+                       int64_t n, int hidden, int inter, uint16_t* y,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * One sparse-MoE layer: router -> permute -> experts -> weighted combine,
+ * with no host synchronisation.  Replaces MoELayer._forward_tokens
+ * (model/moe_layer.py:117-211) for GPU-resident experts: routing
+ * (:143), per-expert masked dispatch in ascending expert id (:150-186) and
+ * output[mask] += y * w with one fp16 rounding per expert (:187-191).
+ *   h fp16 [T, hidden], wg fp16 [E, hidden], experts[E] (host array)
+ *   out fp16 [T, hidden]; indices int64 [T, k] and weights fp32 [T, k]
+ *   receive the routing (both required).
+ */
+size_t moe_layer_workspace_size(int64_t T, int hidden, int inter, int E, int k);
+int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
+                      const moe_nf4_expert_t* experts, int E, int k, int64_t T,
+                      int hidden, int inter, uint16_t* out, int64_t* indices,
+                      float* weights, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Building blocks of moe_layer_forward, exported for tests and for the
+ * expert-parallel path (dispatch/combine around an all-to-all).
+ *
+ * moe_permute: stable counting sort of the T*k (token, slot) pairs by expert.
+ *   expert_offsets int32 [E+1]; pair_token int32 [T*k] (token of each sorted
+ *   pair, ascending token order within an expert); pair_weight fp32 [T*k];
+ *   pair_slot int32 [T*k] (sorted position of pair t*k+j).
+ * (model/moe_layer.py:172-185: mask = any(idx == e), h[mask] in token order.)
+ */
+int moe_permute(const int64_t* indices, const float* weights, int64_t T, int k,
+                int E, int32_t* expert_offsets, int32_t* pair_token,
+                float* pair_weight, int32_t* pair_slot, void* stream);
+
+/* rows_out[i] = rows_in[index[i]] for fp16 rows of width `width`. */
+int moe_gather_rows(const uint16_t* rows_in, const int32_t* index, int64_t n,
+                    int width, uint16_t* rows_out, void* stream);
+
+/* Weighted combine in ascending expert order, one fp16 rounding per expert
+ * (model/moe_layer.py:187-191):
+ *   out[t] = fp16(out[t] + fp32(y[pair_slot[t*k+j]]) * w[t,j]) for the token's
+ *   experts in ascending id, starting from out[t] = 0. */
+int moe_combine(const uint16_t* y_sorted, const int32_t* pair_slot,
+                const int64_t* indices, const float* weights, int64_t T, int k,
+                int width, uint16_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H */

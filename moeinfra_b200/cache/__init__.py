@@ -1,0 +1,1 @@
+"""cache subsystem (B200 rebuild of the reference package of the same name)."""

@@ -1,0 +1,78 @@
+// Shared device/host helpers for the B200 MoE kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/moe_b200.h"
+
+#define MOE_CHECK_LAUNCH()                                   \
+  do {                                                       \
+    cudaError_t _e = cudaGetLastError();                     \
+    if (_e != cudaSuccess) return MOE_ERR_CUDA;              \
+  } while (0)
+
+namespace moe {
+
+constexpr int kWarp = 32;
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+// fp16 <-> float on raw bit patterns.
+__device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// acc += fp32(a) * fp32(b) for fp16 a, b: the product of two fp16 values is
+// exact in fp32, so this is a single rounding of the sum (sm_100 mixed FMA).
+__device__ __forceinline__ float fma_f16f16_f32(uint16_t a, uint16_t b, float acc) {
+  float d;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(acc));
+  return d;
+}
+
+// Multirow (GEMM-path) weight: fp16(bf16_rn(code * absmax)), product in fp32.
+// Returns the two fp16 weights of one packed byte as a half2 bit pattern
+// (low half = element 2j, high half = element 2j+1).
+__device__ __forceinline__ uint32_t nf4_pair_multirow(float c_even, float c_odd, float absmax) {
+  float p0 = __fmul_rn(c_even, absmax);
+  float p1 = __fmul_rn(c_odd, absmax);
+  __nv_bfloat162 b = __floats2bfloat162_rn(p0, p1);  // .x = p0, .y = p1
+  __half2 h = __floats2half2_rn(__bfloat162float(b.x), __bfloat162float(b.y));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Split a half2 bit pattern into its two fp16 halves.
+__device__ __forceinline__ uint16_t lo16(uint32_t v) { return static_cast<uint16_t>(v & 0xFFFFu); }
+__device__ __forceinline__ uint16_t hi16(uint32_t v) { return static_cast<uint16_t>(v >> 16); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// torch F.silu on fp16 input: x / (1 + exp(-x)) in fp32, rounded to fp16;
+// then (silu(g) * u) in fp32 rounded to fp16 (nf4_reconstruct.py:152-155).
+__device__ __forceinline__ uint16_t swiglu_f16(uint16_t g16, uint16_t u16) {
+  float g = h2f(g16);
+  float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+  uint16_t s16 = f2h(s);
+  return f2h(__fmul_rn(h2f(s16), h2f(u16)));
+}
+
+}  // namespace moe

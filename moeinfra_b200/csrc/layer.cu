@@ -1,0 +1,204 @@
+// Host orchestration of the fused MoE layer and of the single-expert forward.
+//
+// moe_layer_forward replaces MoELayer._forward_tokens (model/moe_layer.py:117-211)
+// for GPU-resident experts: one routing pass (:143), per-expert dispatch in
+// ascending expert id over the tokens routed to it (:150-186) and the weighted
+// fp16 combine (:187-191) -- as a fixed launch sequence on one stream with no
+// device->host synchronisation (the reference syncs on unique().tolist(),
+// :150-153).  Every buffer comes from the caller's workspace.
+#include "common.cuh"
+
+namespace moe {
+
+// expert_decode.cu
+void decode_split(int inter, int* S, int* split_chunks);
+int decode_max_tokens();
+int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t* expert_offsets,
+                          const int32_t* pair_token, const uint16_t* x, int hidden, int inter,
+                          uint16_t* h_sorted, float* y_part, int S, int split_chunks,
+                          cudaStream_t s);
+int launch_reduce_partials(const float* part, int64_t P, int S, int width, uint16_t* y,
+                           cudaStream_t s);
+int launch_identity_offsets(int32_t* off, int n, cudaStream_t s);
+// permute.cu
+int launch_permute(const int64_t* indices, const float* weights, int64_t T, int k, int E,
+                   int32_t* expert_offsets, int32_t* pair_token, float* pair_weight,
+                   int32_t* pair_slot, cudaStream_t s);
+int launch_combine_partials(const float* part, int S, const int32_t* pair_slot,
+                            const int64_t* indices, const float* weights, int64_t T, int k,
+                            int width, uint16_t* out, cudaStream_t s);
+// expert_gemm_sm100.cu
+int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
+                                const int32_t* expert_offsets, const uint16_t* x_sorted,
+                                int64_t P, int hidden, int inter, uint16_t* h_sorted,
+                                uint16_t* y_sorted, cudaStream_t s);
+
+namespace {
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Sequential carve-out of the caller's workspace.
+struct Carver {
+  unsigned char* base;
+  size_t used = 0;
+  template <class T>
+  T* take(size_t count) {
+    T* p = reinterpret_cast<T*>(base ? base + used : nullptr);
+    used += align_up(count * sizeof(T));
+    return p;
+  }
+};
+
+bool use_decode_path(int64_t T) { return T <= decode_max_tokens(); }
+
+struct LayerBufs {
+  int32_t* offsets;
+  int32_t* pair_token;
+  float* pair_weight;
+  int32_t* pair_slot;
+  uint16_t* h_sorted;
+  float* y_part;      // decode path
+  uint16_t* x_sorted;  // grouped-GEMM path
+  uint16_t* y_sorted;  // grouped-GEMM path
+};
+
+size_t carve_layer(unsigned char* ws, int64_t T, int hidden, int inter, int E, int k,
+                   LayerBufs* b) {
+  Carver c{ws};
+  const int64_t P = T * k;
+  b->offsets = c.take<int32_t>(E + 1);
+  b->pair_token = c.take<int32_t>(P);
+  b->pair_weight = c.take<float>(P);
+  b->pair_slot = c.take<int32_t>(P);
+  b->h_sorted = c.take<uint16_t>((size_t)P * inter);
+  if (use_decode_path(T)) {
+    int S, sc;
+    decode_split(inter, &S, &sc);
+    b->y_part = c.take<float>((size_t)P * S * hidden);
+    b->x_sorted = b->y_sorted = nullptr;
+  } else {
+    b->y_part = nullptr;
+    b->x_sorted = c.take<uint16_t>((size_t)P * hidden);
+    b->y_sorted = c.take<uint16_t>((size_t)P * hidden);
+  }
+  return c.used;
+}
+
+bool shapes_ok(int hidden, int inter) {
+  return hidden > 0 && inter > 0 && hidden % 128 == 0 && inter % 128 == 0;
+}
+
+bool experts_aligned(const moe_nf4_expert_t* ex, int E) {
+  for (int e = 0; e < E; ++e) {
+    const moe_nf4_matrix_t* m[3] = {&ex[e].w1, &ex[e].w3, &ex[e].w2};
+    for (auto* mm : m) {
+      if (!mm->q || !mm->absmax || !mm->code) return false;
+      if (!aligned16(mm->q)) return false;
+    }
+  }
+  return true;
+}
+
+}  // namespace
+}  // namespace moe
+
+extern "C" size_t moe_layer_workspace_size(int64_t T, int hidden, int inter, int E, int k) {
+  moe::LayerBufs b;
+  if (T < 0 || E < 1 || k < 1) return 0;
+  return moe::carve_layer(nullptr, T, hidden, inter, E, k, &b);
+}
+
+extern "C" int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
+                                 const moe_nf4_expert_t* experts, int E, int k, int64_t T,
+                                 int hidden, int inter, uint16_t* out, int64_t* indices,
+                                 float* weights, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  using namespace moe;
+  if (T < 0 || E < 1 || E > MOE_MAX_EXPERTS || k < 1 || k > E || k > 8) return MOE_ERR_INVALID_ARG;
+  if (!shapes_ok(hidden, inter)) return MOE_ERR_UNSUPPORTED;
+  if (T == 0) return MOE_OK;
+  if (!h || !wg || !experts || !out || !indices || !weights) return MOE_ERR_INVALID_ARG;
+  if (!experts_aligned(experts, E) || !aligned16(h) || !aligned16(out)) return MOE_ERR_ALIGNMENT;
+  LayerBufs b;
+  const size_t need = carve_layer(static_cast<unsigned char*>(workspace), T, hidden, inter, E, k, &b);
+  if (!workspace || workspace_bytes < need) return MOE_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = moe_router_topk(h, wg, T, hidden, E, k, nullptr, weights, indices, s);
+  if (st != MOE_OK) return st;
+  st = launch_permute(indices, weights, T, k, E, b.offsets, b.pair_token, b.pair_weight,
+                      b.pair_slot, s);
+  if (st != MOE_OK) return st;
+  const int64_t P = T * k;
+  if (use_decode_path(T)) {
+    int S, sc;
+    decode_split(inter, &S, &sc);
+    st = launch_decode_experts(experts, E, b.offsets, b.pair_token, h, hidden, inter, b.h_sorted,
+                               b.y_part, S, sc, s);
+    if (st != MOE_OK) return st;
+    return launch_combine_partials(b.y_part, S, b.pair_slot, indices, weights, T, k, hidden, out,
+                                   s);
+  }
+  st = moe_gather_rows(h, b.pair_token, P, hidden, b.x_sorted, s);
+  if (st != MOE_OK) return st;
+  st = launch_grouped_gemm_experts(experts, E, b.offsets, b.x_sorted, P, hidden, inter, b.h_sorted,
+                                   b.y_sorted, s);
+  if (st != MOE_OK) return st;
+  return moe_combine(b.y_sorted, b.pair_slot, indices, weights, T, k, hidden, out, s);
+}
+
+namespace moe {
+namespace {
+struct ExpertBufs {
+  int32_t* offsets;
+  uint16_t* h;
+  float* y_part;
+};
+size_t carve_expert(unsigned char* ws, int64_t n, int hidden, int inter, ExpertBufs* b) {
+  Carver c{ws};
+  b->offsets = c.take<int32_t>(2);
+  b->h = c.take<uint16_t>((size_t)n * inter);
+  if (use_decode_path(n)) {
+    int S, sc;
+    decode_split(inter, &S, &sc);
+    b->y_part = c.take<float>((size_t)n * S * hidden);
+  } else {
+    b->y_part = nullptr;
+  }
+  return c.used;
+}
+}  // namespace
+}  // namespace moe
+
+extern "C" size_t moe_expert_workspace_size(int64_t n, int hidden, int inter) {
+  moe::ExpertBufs b;
+  if (n < 0) return 0;
+  return moe::carve_expert(nullptr, n, hidden, inter, &b);
+}
+
+extern "C" int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t* x, int64_t n,
+                                  int hidden, int inter, uint16_t* y, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  using namespace moe;
+  if (n < 0) return MOE_ERR_INVALID_ARG;
+  if (!shapes_ok(hidden, inter)) return MOE_ERR_UNSUPPORTED;
+  if (n == 0) return MOE_OK;
+  if (!expert || !x || !y) return MOE_ERR_INVALID_ARG;
+  if (!experts_aligned(expert, 1) || !aligned16(x) || !aligned16(y)) return MOE_ERR_ALIGNMENT;
+  if (n > (int64_t)1 << 30) return MOE_ERR_INVALID_ARG;
+  ExpertBufs b;
+  const size_t need = carve_expert(static_cast<unsigned char*>(workspace), n, hidden, inter, &b);
+  if (!workspace || workspace_bytes < need) return MOE_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = launch_identity_offsets(b.offsets, static_cast<int>(n), s);
+  if (st != MOE_OK) return st;
+  if (use_decode_path(n)) {
+    int S, sc;
+    decode_split(inter, &S, &sc);
+    st = launch_decode_experts(expert, 1, b.offsets, nullptr, x, hidden, inter, b.h, b.y_part, S,
+                               sc, s);
+    if (st != MOE_OK) return st;
+    return launch_reduce_partials(b.y_part, n, S, hidden, y, s);
+  }
+  return launch_grouped_gemm_experts(expert, 1, b.offsets, x, n, hidden, inter, b.h, y, s);
+}

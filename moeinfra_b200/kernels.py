@@ -1,0 +1,212 @@
+"""Torch-facing wrappers of the C ABI (device memory and streams come from torch).
+
+Every function validates dtype, device and contiguity the way the reference's
+Python layer does, allocates outputs and workspace with the torch caching
+allocator, enqueues on the current CUDA stream and raises ``RuntimeError``
+with the library's status text on failure.  There is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Sequence
+
+import torch
+
+from moeinfra_b200 import _native
+from moeinfra_b200._native import NF4Expert, NF4Matrix, check
+
+NF4_BLOCKSIZE = 64
+NESTED_BLOCKSIZE = 256
+
+
+def _p(t: torch.Tensor | None) -> ctypes.c_void_p | None:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _need_cuda(what: str, **tensors: torch.Tensor) -> torch.device:
+    dev = None
+    for name, t in tensors.items():
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{what}: {name} must be a torch.Tensor")
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                f"{what}: {name} is on {t.device}; the B200 kernels run on CUDA tensors only "
+                "(there is no CPU path)")
+        if not t.is_contiguous():
+            raise ValueError(f"{what}: {name} must be contiguous")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"{what}: {name} is on {t.device}, expected {dev}")
+    assert dev is not None
+    return dev
+
+
+def _need_dtype(what: str, t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if t.dtype != dtype:
+        raise ValueError(f"{what}: {name} must be {dtype}, got {t.dtype}")
+
+
+def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+# ---------------------------------------------------------------------------
+# NF4 dequant
+# ---------------------------------------------------------------------------
+
+def nf4_dequant(q: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, numel: int,
+                blocksize: int = NF4_BLOCKSIZE) -> torch.Tensor:
+    """bf16 ``code[nib(i)] * absmax[i // blocksize]`` (bit-exact), flat [numel]."""
+    dev = _need_cuda("nf4_dequant", q=q, absmax=absmax, code=code)
+    _need_dtype("nf4_dequant", q, torch.uint8, "q")
+    _need_dtype("nf4_dequant", absmax, torch.float32, "absmax")
+    _need_dtype("nf4_dequant", code, torch.float32, "code")
+    if q.numel() * 2 < numel or absmax.numel() * blocksize < numel or code.numel() < 16:
+        raise ValueError("nf4_dequant: buffers too small for numel")
+    out = torch.empty(numel, dtype=torch.bfloat16, device=dev)
+    check(_native.lib().moe_nf4_dequant(_p(q), _p(absmax), _p(code), numel, blocksize, _p(out),
+                                        _stream(dev)), "moe_nf4_dequant")
+    return out
+
+
+def nested_absmax(qabs: torch.Tensor, absmax2: torch.Tensor, code2: torch.Tensor,
+                  offset: float, blocksize2: int = NESTED_BLOCKSIZE) -> torch.Tensor:
+    dev = _need_cuda("nested_absmax", qabs=qabs, absmax2=absmax2, code2=code2)
+    _need_dtype("nested_absmax", qabs, torch.uint8, "qabs")
+    _need_dtype("nested_absmax", absmax2, torch.float32, "absmax2")
+    _need_dtype("nested_absmax", code2, torch.float32, "code2")
+    n = qabs.numel()
+    if absmax2.numel() * blocksize2 < n or code2.numel() < 256:
+        raise ValueError("nested_absmax: nested state too small")
+    out = torch.empty(n, dtype=torch.float32, device=dev)
+    check(_native.lib().moe_nf4_nested_absmax(_p(qabs), _p(absmax2), _p(code2), float(offset), n,
+                                              blocksize2, _p(out), _stream(dev)),
+          "moe_nf4_nested_absmax")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Router
+# ---------------------------------------------------------------------------
+
+def router_topk(h: torch.Tensor, wg: torch.Tensor, k: int, with_logits: bool = True):
+    """``(logits fp16 [T,E] | None, weights fp32 [T,k], indices int64 [T,k])``."""
+    dev = _need_cuda("router_topk", h=h, wg=wg)
+    _need_dtype("router_topk", h, torch.float16, "hidden_states")
+    _need_dtype("router_topk", wg, torch.float16, "gate_weight")
+    T, H = h.shape
+    E = wg.shape[0]
+    logits = torch.empty(T, E, dtype=torch.float16, device=dev) if with_logits else None
+    w = torch.empty(T, k, dtype=torch.float32, device=dev)
+    idx = torch.empty(T, k, dtype=torch.int64, device=dev)
+    check(_native.lib().moe_router_topk(_p(h), _p(wg), T, H, E, k, _p(logits), _p(w), _p(idx),
+                                        _stream(dev)), "moe_router_topk")
+    return logits, w, idx
+
+
+def router_topk_from_logits(logits: torch.Tensor, k: int):
+    dev = _need_cuda("router_topk_from_logits", logits=logits)
+    _need_dtype("router_topk_from_logits", logits, torch.float16, "logits")
+    T, E = logits.shape
+    w = torch.empty(T, k, dtype=torch.float32, device=dev)
+    idx = torch.empty(T, k, dtype=torch.int64, device=dev)
+    check(_native.lib().moe_router_topk_from_logits(_p(logits), T, E, k, _p(w), _p(idx),
+                                                    _stream(dev)), "moe_router_topk_from_logits")
+    return w, idx
+
+
+# ---------------------------------------------------------------------------
+# Experts and the fused layer
+# ---------------------------------------------------------------------------
+
+def matrix_desc(q: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor) -> NF4Matrix:
+    return NF4Matrix(q.data_ptr(), absmax.data_ptr(), code.data_ptr())
+
+
+def expert_forward(desc: NF4Expert, x: torch.Tensor, hidden: int, inter: int) -> torch.Tensor:
+    dev = _need_cuda("expert_forward", x=x)
+    _need_dtype("expert_forward", x, torch.float16, "x")
+    if x.ndim != 2 or x.shape[1] != hidden:
+        raise ValueError(f"expert_forward: x must be [n, {hidden}], got {tuple(x.shape)}")
+    n = x.shape[0]
+    y = torch.empty(n, hidden, dtype=torch.float16, device=dev)
+    lib = _native.lib()
+    ws_bytes = lib.moe_expert_workspace_size(n, hidden, inter)
+    ws = _workspace(ws_bytes, dev)
+    check(lib.moe_expert_forward(ctypes.byref(desc), _p(x), n, hidden, inter, _p(y), _p(ws),
+                                 ws_bytes, _stream(dev)), "moe_expert_forward")
+    return y
+
+
+def expert_array(descs: Sequence[NF4Expert]):
+    arr = (NF4Expert * len(descs))()
+    for i, d in enumerate(descs):
+        arr[i] = d
+    return arr
+
+
+def layer_forward(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hidden: int, inter: int,
+                  out: torch.Tensor | None = None):
+    """Fused MoE layer: returns ``(out fp16 [T,H], indices int64 [T,k], weights fp32 [T,k])``.
+
+    ``experts`` is a ctypes array of ``NF4Expert`` (see :func:`expert_array`).
+    """
+    dev = _need_cuda("layer_forward", h=h, wg=wg)
+    _need_dtype("layer_forward", h, torch.float16, "hidden_states")
+    _need_dtype("layer_forward", wg, torch.float16, "gate_weight")
+    T = h.shape[0]
+    E = len(experts)
+    if out is None:
+        out = torch.empty(T, hidden, dtype=torch.float16, device=dev)
+    idx = torch.empty(T, k, dtype=torch.int64, device=dev)
+    w = torch.empty(T, k, dtype=torch.float32, device=dev)
+    lib = _native.lib()
+    ws_bytes = lib.moe_layer_workspace_size(T, hidden, inter, E, k)
+    ws = _workspace(ws_bytes, dev)
+    check(lib.moe_layer_forward(_p(h), _p(wg), experts, E, k, T, hidden, inter, _p(out), _p(idx),
+                                _p(w), _p(ws), ws_bytes, _stream(dev)), "moe_layer_forward")
+    return out, idx, w
+
+
+def permute(indices: torch.Tensor, weights: torch.Tensor, num_experts: int):
+    dev = _need_cuda("permute", indices=indices, weights=weights)
+    _need_dtype("permute", indices, torch.int64, "indices")
+    _need_dtype("permute", weights, torch.float32, "weights")
+    T, k = indices.shape
+    P = T * k
+    offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    pair_token = torch.empty(P, dtype=torch.int32, device=dev)
+    pair_weight = torch.empty(P, dtype=torch.float32, device=dev)
+    pair_slot = torch.empty(P, dtype=torch.int32, device=dev)
+    check(_native.lib().moe_permute(_p(indices), _p(weights), T, k, num_experts, _p(offsets),
+                                    _p(pair_token), _p(pair_weight), _p(pair_slot), _stream(dev)),
+          "moe_permute")
+    return offsets, pair_token, pair_weight, pair_slot
+
+
+def gather_rows(rows: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    dev = _need_cuda("gather_rows", rows=rows, index=index)
+    _need_dtype("gather_rows", rows, torch.float16, "rows")
+    _need_dtype("gather_rows", index, torch.int32, "index")
+    out = torch.empty(index.numel(), rows.shape[1], dtype=torch.float16, device=dev)
+    check(_native.lib().moe_gather_rows(_p(rows), _p(index), index.numel(), rows.shape[1], _p(out),
+                                        _stream(dev)), "moe_gather_rows")
+    return out
+
+
+def combine(y_sorted: torch.Tensor, pair_slot: torch.Tensor, indices: torch.Tensor,
+            weights: torch.Tensor) -> torch.Tensor:
+    dev = _need_cuda("combine", y_sorted=y_sorted, pair_slot=pair_slot, indices=indices,
+                     weights=weights)
+    _need_dtype("combine", y_sorted, torch.float16, "y_sorted")
+    T, k = indices.shape
+    width = y_sorted.shape[1]
+    out = torch.empty(T, width, dtype=torch.float16, device=dev)
+    check(_native.lib().moe_combine(_p(y_sorted), _p(pair_slot), _p(indices), _p(weights), T, k,
+                                    width, _p(out), _stream(dev)), "moe_combine")
+    return out

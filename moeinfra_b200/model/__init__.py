@@ -1,0 +1,1 @@
+"""model subsystem (B200 rebuild of the reference package of the same name)."""

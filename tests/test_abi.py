@@ -1,0 +1,79 @@
+"""CPU: the C-ABI library loads and exports every entry point of include/*.h.
+
+No kernel is launched here; calls below only exercise host-side argument
+validation, which returns before any CUDA work is enqueued.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from moeinfra_b200 import _native
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared_functions() -> set[str]:
+    names = set()
+    for hdr in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", hdr.read_text(), flags=re.S)
+        for m in re.finditer(r"\b(moe_[a-z0-9_]+)\s*\(", text):
+            names.add(m.group(1))
+    return names
+
+
+def test_library_loads():
+    lib = _native.lib()
+    assert lib.moe_version().decode().startswith("moe_b200")
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    lib = _native.lib()
+    declared = _declared_functions()
+    assert {"moe_nf4_dequant", "moe_router_topk", "moe_layer_forward", "moe_expert_forward"} <= declared
+    for name in declared:
+        assert hasattr(lib, name), f"{name} missing from libmoe_b200.so"
+    assert declared <= set(_native.SIGNATURES), "ctypes signatures out of date with the header"
+
+
+def test_status_strings():
+    for code in range(7):
+        assert _native.status_string(code) != "unknown status"
+    assert _native.status_string(99) == "unknown status"
+
+
+def test_workspace_sizes_grow_with_tokens():
+    lib = _native.lib()
+    a = lib.moe_layer_workspace_size(1, 4096, 14336, 8, 2)
+    b = lib.moe_layer_workspace_size(64, 4096, 14336, 8, 2)
+    c = lib.moe_layer_workspace_size(4096, 4096, 14336, 8, 2)
+    assert 0 < a < b < c
+    assert lib.moe_expert_workspace_size(16, 4096, 14336) > lib.moe_expert_workspace_size(1, 4096, 14336)
+
+
+def test_host_validation_rejects_bad_arguments_without_launching():
+    lib = _native.lib()
+    # odd numel / bad blocksize / null pointers -> invalid argument
+    assert lib.moe_nf4_dequant(None, None, None, 3, 64, None, None) == 1
+    assert lib.moe_nf4_dequant(None, None, None, 64, 48, None, None) == 1
+    assert lib.moe_router_topk(None, None, 4, 4096, 33, 2, None, None, None, None) == 1
+    assert lib.moe_router_topk(None, None, 4, 4096, 8, 9, None, None, None, None) == 1
+    # unsupported shapes
+    desc = _native.NF4Expert()
+    assert lib.moe_expert_forward(ctypes.byref(desc), None, 1, 100, 14336, None, None, 0, None) == 2
+    # zero-size work is a no-op success
+    assert lib.moe_nf4_dequant(None, None, None, 0, 64, None, None) == 0
+    assert lib.moe_router_topk(None, None, 0, 4096, 8, 2, None, None, None, None) == 0
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setenv("MOE_B200_LIB", str(tmp_path / "nope.so"))
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _native.lib()
+    monkeypatch.delenv("MOE_B200_LIB")
+    monkeypatch.setattr(_native, "_lib", None)
+    _native.lib()
