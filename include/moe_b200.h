@@ -41,11 +41,12 @@ typedef enum moe_status {
 #define MOE_MAX_EXPERTS 16
 #define MOE_NF4_BLOCKSIZE 64
 
-/* One NF4-quantized linear layer [rows=out, cols=in] in store layout. */
+/* One resident NF4-quantized linear layer [rows=out, cols=in] in the tile16
+ * device layout (see moe_nf4_tile16): rows % 16 == 0, cols % 64 == 0. */
 typedef struct moe_nf4_matrix {
-  const uint8_t* q;     /* packed codes, rows*cols/2 bytes, 16-byte aligned */
-  const float* absmax;  /* fp32, rows*cols/64 (already de-nested)          */
-  const float* code;    /* fp32[16] codebook (the store's quant_map)        */
+  const uint8_t* q;     /* packed codes, rows*cols/2 bytes, tile16, 16-byte aligned */
+  const float* absmax;  /* fp32, rows*cols/64, tile16 order (already de-nested)    */
+  const float* code;    /* fp32[16] codebook (the store's quant_map)               */
 } moe_nf4_matrix_t;
 
 /* One Mixtral SwiGLU expert: w1, w3 are [inter, hidden]; w2 is [hidden, inter]. */
@@ -61,6 +62,11 @@ const char* moe_status_string(int status);
 /* Library build identifier (static storage). */
 const char* moe_version(void);
 
+/* Reads and clears the device-side error word that kernels set when one of
+ * their bounded waits (bulk-copy pipeline barriers) times out.  Synchronous
+ * (a device-to-host copy).  *value is 0 when no wait timed out. */
+int moe_take_device_error(int* value);
+
 /* ---------------------------------------------------------------------------
  * NF4 blockwise dequant to bf16, bit-exact:
  *   out[i] = bf16_rn(code[nib(i)] * absmax[i / blocksize])   (fp32 product)
@@ -71,6 +77,27 @@ const char* moe_version(void);
 int moe_nf4_dequant(const uint8_t* q, const float* absmax, const float* code,
                     int64_t numel, int blocksize, uint16_t* out_bf16,
                     void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Store layout -> tile16 device layout (exact permutation of bytes and words).
+ * Store: row-major [rows, cols], element 2j in the high nibble of byte j, one
+ * absmax per 64 consecutive elements of a row.  tile16: for row tile rb (16
+ * rows) and 64-element block kb, the 16 rows' 32-byte block segments are
+ * contiguous:
+ *   q_out byte   ((rb*(cols/64) + kb)*16 + r)*32 + j = q row 16rb+r, block kb, byte j
+ *   absmax_out   ((rb*(cols/64) + kb)*16 + r)        = absmax row 16rb+r, block kb
+ * Used when an expert becomes GPU-resident (the reference's reconstruct step,
+ * transfer/nf4_reconstruct.py:117-150).  rows % 16 == 0, cols % 64 == 0.
+ */
+int moe_nf4_tile16(const uint8_t* q, const float* absmax, int64_t rows,
+                   int64_t cols, uint8_t* q_out, float* absmax_out,
+                   void* stream);
+
+/* bf16(code * absmax) of a tile16 matrix, written row-major [rows, cols];
+ * bit-exact with moe_nf4_dequant on the store layout. */
+int moe_nf4_dequant_tile16(const uint8_t* q, const float* absmax,
+                           const float* code, int64_t rows, int64_t cols,
+                           uint16_t* out_bf16, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Rebuild fp32 absmax from its double quantization (nested QuantState,
@@ -107,8 +134,8 @@ int moe_router_topk_from_logits(const uint16_t* logits, int64_t T, int E,
  * with the bitsandbytes Linear4bit path it reaches: n == 1 uses the 4-bit
  * GEMV semantics (fp16(fp16(code)*fp16(absmax)) weights), n > 1 the
  * dequant-to-bf16-then-fp16-GEMM semantics.
- *   x fp16 [n, hidden]  ->  y fp16 [n, hidden]
- * Requires hidden % 128 == 0 and inter % 128 == 0.
+ *   x fp16 [n, hidden]  ->  y fp16 [n, hidden]; weights in tile16 layout.
+ * Requires hidden % 64 == 0 (<= 8192) and inter % 64 == 0.
  */
 size_t moe_expert_workspace_size(int64_t n, int hidden, int inter);
 int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t* x,

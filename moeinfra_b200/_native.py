@@ -28,7 +28,11 @@ class NF4Expert(ctypes.Structure):
 SIGNATURES: dict[str, tuple] = {
     "moe_status_string": (ctypes.c_char_p, [c_int]),
     "moe_version": (ctypes.c_char_p, []),
+    "moe_take_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "moe_nf4_dequant": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "moe_nf4_tile16": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
+    "moe_nf4_dequant_tile16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+                                       c_void_p]),
     "moe_nf4_nested_absmax": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_int64, c_int,
                                       c_void_p, c_void_p]),
     "moe_router_topk": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p,
@@ -76,6 +80,13 @@ def lib() -> ctypes.CDLL:
 
 def status_string(status: int) -> str:
     return lib().moe_status_string(int(status)).decode()
+
+
+def take_device_error() -> int:
+    """Read and clear the device error word (1 = a bounded kernel wait timed out)."""
+    v = c_int(0)
+    check(lib().moe_take_device_error(ctypes.byref(v)), "moe_take_device_error")
+    return v.value
 
 
 def check(status: int, what: str) -> None:

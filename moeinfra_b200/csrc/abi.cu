@@ -15,3 +15,19 @@ extern "C" const char* moe_status_string(int status) {
 }
 
 extern "C" const char* moe_version(void) { return "moe_b200 sm_100a 0.1"; }
+
+namespace moe {
+// Set to 1 by any kernel whose bounded wait timed out; read and cleared by
+// moe_take_device_error().
+__device__ int g_wait_error = 0;
+}  // namespace moe
+
+extern "C" int moe_take_device_error(int* value) {
+  if (!value) return MOE_ERR_INVALID_ARG;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, moe::g_wait_error, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(moe::g_wait_error, &zero, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
+  *value = v;
+  return MOE_OK;
+}

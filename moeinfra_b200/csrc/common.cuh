@@ -18,6 +18,11 @@ namespace moe {
 
 constexpr int kWarp = 32;
 
+// Expert descriptors passed by value as a kernel parameter.
+struct ExpertTable {
+  moe_nf4_expert_t e[MOE_MAX_EXPERTS];
+};
+
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -1,302 +1,473 @@
-// Decode-path SwiGLU experts on packed NF4 weights (few tokens per expert).
+// Decode-path SwiGLU experts (1..8 tokens per expert) on tile16 NF4 weights.
 //
-// Reference: ReconstructedNF4Expert.forward (transfer/nf4_reconstruct.py:152-155)
-//   y = w2(silu(w1 x) * w3 x), each wN a bitsandbytes Linear4bit in fp16
-//   compute (:94).  bitsandbytes' matmul_4bit takes the 4-bit GEMV for a
-//   single input row and dequant(bf16)->fp16 GEMM otherwise; the kernels
-//   below pick the same semantics per expert from its device-side token count:
-//     1 token : w = fp16(fp16(code) * fp16(absmax)), acc += fp32(x)*fp32(w)
-//     n > 1   : w = fp16(bf16(code * absmax)),       acc += fp32(x)*fp32(w)
-//   and round each output once to fp16.
+// Reference: ReconstructedNF4Expert.forward (transfer/nf4_reconstruct.py:152-155),
+// y = w2(silu(w1 x) * w3 x) with three bitsandbytes Linear4bit layers in fp16
+// compute (:94).  bitsandbytes takes its 4-bit GEMV for a single input row
+// and dequant(bf16) -> fp16 GEMM otherwise; the kernels pick per expert from
+// its device-side token count n:
+//   n == 1 ("gemv"):  y_row += absmax_b * sum_{i in block b} fp16(code_i) * x_i
+//                     (absmax in fp32 per 64-element block; bitsandbytes rounds
+//                     fp16(code)*fp16(absmax) per weight instead);
+//   n >= 2 ("multi"): w_i = fp16(bf16(code_i * absmax_b)), y = sum w_i x_i;
+// exact fp16 products, fp32 accumulation, outputs rounded once to fp16.
 //
-// Work split (HBM-bound streaming of packed rows):
-//   gate_up : CTA item = (expert, 64 rows of W1 and W3); a warp owns whole
-//             row pairs so SwiGLU is formed in registers; x of the expert's
-//             tokens is staged once per item in shared memory.
-//   down    : CTA item = (expert, K-split, 64 rows of W2); split-K over the
-//             14336-long reduction for load balance; fp32 partials are summed
-//             in split order by the combine kernel (deterministic).
-// Each lane loads 16 packed bytes (32 weights) per 128-bit load.  Bytes are
-// decoded through shared-memory tables indexed by the whole byte, replicated
-// per bank so random bytes never conflict: lut16 (half2 of the two fp16
-// codes, 32 KB) for the 1-token semantics, lut32 (float2 of the two fp32
-// codes, 32 KB) for the multi-token semantics.
+// Design (HBM-bound streaming, no weight byte read twice):
+//   * weights are in the tile16 layout (nf4_layout.cu): per 64-element block a
+//     thread (g = lane/4, t = lane%4) loads 8 bytes of MMA row g and of row
+//     g+8, and the warp's loads are 256 contiguous bytes; streaming loads go
+//     straight to registers (weights never touch shared memory, which is kept
+//     for the decode table);
+//   * packed bytes index a shared-memory table placed at shared-window address
+//     0x10000: entry (byte, lane) is the byte's two fp16 codes (32 bank
+//     replicas) and, at +128, its two fp32 codes (16 replicas), so the address
+//     is a single byte-permute of the packed word;
+//   * the multiply-adds are m16n8k16 MMAs.  MMA j of a block takes bytes 2j,
+//     2j+1 (elements 16t+4j..16t+4j+3) as virtual K columns 2t,2t+1 /
+//     2t+8,2t+9, which makes the B fragment exactly the thread's own x words;
+//     B column g carries token g (n > 1) or the single token (n == 1);
+//   * 16 warps per CTA split K; their partials meet in shared memory in warp
+//     order (deterministic).
+//   gate_up: item = 8 rows; MMA rows 0..7 are W1 rows, 8..15 the same W3 rows,
+//            so g and u of a (row, token) end up in one thread.
+//   down   : item = (16 rows, K split s of 2048 elements); split partials go
+//            to y_part[slot][S][H] and the combine kernel sums them in order.
 #include "common.cuh"
 
 namespace moe {
-
-struct ExpertTable {
-  moe_nf4_expert_t e[MOE_MAX_EXPERTS];
-};
-
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kRowsPerItem = 64;  // rows per CTA work item
-constexpr int kMaxTok = 4;        // tokens per expert handled by this path
-constexpr int kLut16Words = 256 * 32;
-constexpr int kLut32Pairs = 256 * 16;
+constexpr int kWarpsK = 16;           // warps per CTA, each a K part
+constexpr int kThreadsK = kWarpsK * 32;
+constexpr int kMaxTok = 8;            // tokens per expert on this path
+constexpr int kDownSlice = 2048;      // K elements per down split
+constexpr uint32_t kLutWin = 0x10000;
+constexpr int kDynSmem = 0x20000;     // dynamic allocation covering the window
 
 struct DecodeArgs {
   ExpertTable ex;
   int E;
-  const int32_t* expert_offsets;  // [E+1] device
-  const int32_t* pair_token;      // [P] token row in x for each sorted pair, or null (identity)
-  const uint16_t* x;              // fp16 rows [*, H]
+  const int32_t* expert_offsets;  // [E+1]
+  const int32_t* pair_token;      // token row of each sorted pair (or null: identity)
+  const uint16_t* x;              // fp16 input rows [*, H]
   uint16_t* h_sorted;             // fp16 [P, I]
   float* y_part;                  // fp32 [P][S][H]
-  int H, I, S, split_chunks;
+  int H, I, S;
 };
 
-__device__ __forceinline__ void build_luts(const float* __restrict__ code, bool need16, bool need32,
-                                           uint32_t* lut16, float2* lut32) {
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float2 lds64f(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint2 ldg_stream64(const uint8_t* p) {
+  return __ldcs(reinterpret_cast<const uint2*>(p));
+}
+// Hint: pull [p, p + bytes) into L2 (bytes a multiple of 16, p 16-byte aligned).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Contiguous item range [begin, end) of this CTA (neighbouring items share
+// tiles, so upcoming tiles are contiguous ranges worth prefetching).
+__device__ __forceinline__ void cta_range(int total, int* begin, int* end) {
+  const int64_t b = (int64_t)total * blockIdx.x / gridDim.x;
+  const int64_t e = (int64_t)total * (blockIdx.x + 1) / gridDim.x;
+  *begin = static_cast<int>(b);
+  *end = static_cast<int>(e);
+}
+
+constexpr int kPrefetchItems = 4;  // L2 prefetch distance in items
+
+template <int K>
+__device__ __forceinline__ uint32_t perm_addr(uint32_t w, uint32_t base) {
+  return __byte_perm(w, base, 0x7604u | (K << 4));
+}
+
+// A-fragment register (fp16 pair) of byte K of w.
+template <bool kMulti, int K>
+__device__ __forceinline__ uint32_t decode(uint32_t w, uint32_t base, float absmax) {
+  if (kMulti) {
+    const float2 c = lds64f(perm_addr<K>(w, base));
+    return nf4_pair_multirow(c.x, c.y, absmax);
+  } else {
+    return lds32(perm_addr<K>(w, base));
+  }
+}
+
+__device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 64-element block into d (rows g, g+8; columns 2t, 2t+1).
+template <bool kMulti>
+__device__ __forceinline__ void block_mma(uint2 qa, uint2 qb, float sa, float sb, const uint32_t* xw,
+                                          uint32_t base, float* d) {
+  mma16816(d, decode<kMulti, 0>(qa.x, base, sa), decode<kMulti, 0>(qb.x, base, sb),
+           decode<kMulti, 1>(qa.x, base, sa), decode<kMulti, 1>(qb.x, base, sb), xw[0], xw[1]);
+  mma16816(d, decode<kMulti, 2>(qa.x, base, sa), decode<kMulti, 2>(qb.x, base, sb),
+           decode<kMulti, 3>(qa.x, base, sa), decode<kMulti, 3>(qb.x, base, sb), xw[2], xw[3]);
+  mma16816(d, decode<kMulti, 0>(qa.y, base, sa), decode<kMulti, 0>(qb.y, base, sb),
+           decode<kMulti, 1>(qa.y, base, sa), decode<kMulti, 1>(qb.y, base, sb), xw[4], xw[5]);
+  mma16816(d, decode<kMulti, 2>(qa.y, base, sa), decode<kMulti, 2>(qb.y, base, sb),
+           decode<kMulti, 3>(qa.y, base, sa), decode<kMulti, 3>(qb.y, base, sb), xw[6], xw[7]);
+}
+
+__device__ __forceinline__ bool build_lut(const float* __restrict__ code, const void* dyn) {
   __shared__ float s_code[16];
+  const uint32_t base = smem_u32(dyn);
+  const bool ok = base <= kLutWin && base + kDynSmem >= kLutWin + 0x10000;
   if (threadIdx.x < 16) s_code[threadIdx.x] = code[threadIdx.x];
   __syncthreads();
-  if (need16) {
-    for (int i = threadIdx.x; i < kLut16Words; i += blockDim.x) {
-      const int v = i >> 5;
-      __half2 h = __floats2half2_rn(s_code[v >> 4], s_code[v & 15]);
-      lut16[i] = *reinterpret_cast<uint32_t*>(&h);
-    }
-  }
-  if (need32) {
-    for (int i = threadIdx.x; i < kLut32Pairs; i += blockDim.x) {
-      const int v = i >> 4;
-      lut32[i] = make_float2(s_code[v >> 4], s_code[v & 15]);
+  if (ok) {
+    for (int i = threadIdx.x; i < 256 * 64; i += blockDim.x) {
+      const int v = i >> 6, j = i & 63;
+      uint32_t val;
+      if (j < 32) {
+        __half2 h = __floats2half2_rn(s_code[v >> 4], s_code[v & 15]);
+        val = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        val = __float_as_uint((j & 1) ? s_code[v & 15] : s_code[v >> 4]);
+      }
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(kLutWin + v * 256 + j * 4), "r"(val));
     }
   }
   __syncthreads();
+  return ok;
 }
 
-// Swizzled shared layout of fp16 rows: chunk c (32 halves = 4 x 16 B) stores
-// its logical 16-byte segment g at physical segment (g + (c >> 1)) & 3, so
-// the 8 lanes of a 128-bit wavefront (chunks l, l+1, ...) hit distinct banks.
-__device__ __forceinline__ int xs_index(int c, int g) { return c * 4 + ((g + (c >> 1)) & 3); }
-
-// Dot products of one 16-byte packed chunk (32 weights) against n tokens.
-template <bool kGemv>
-__device__ __forceinline__ void chunk_dot(const uint4& qv, float absmax, const uint32_t* lut16_l,
-                                          const float2* lut32_l, const uint4* xs, int xs_stride,
-                                          int c, int n, float* acc) {
-  const uint32_t w4[4] = {qv.x, qv.y, qv.z, qv.w};
-  if (kGemv) {
-    const __half a16 = __float2half_rn(absmax);
-    const __half2 a2 = __halves2half2(a16, a16);
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const uint4 xv = xs[xs_index(c, g)];
-      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t byte = (w4[g] >> (8 * b)) & 0xFFu;
-        uint32_t cw = lut16_l[byte * 32];
-        __half2 w = __hmul2(*reinterpret_cast<__half2*>(&cw), a2);
-        const uint32_t wv = *reinterpret_cast<uint32_t*>(&w);
-        acc[0] = fma_f16f16_f32(lo16(xw[b]), lo16(wv), acc[0]);
-        acc[0] = fma_f16f16_f32(hi16(xw[b]), hi16(wv), acc[0]);
-      }
-    }
-  } else {
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      uint4 xv[kMaxTok];
-#pragma unroll
-      for (int t = 0; t < kMaxTok; ++t)
-        xv[t] = (t < n) ? xs[t * xs_stride + xs_index(c, g)] : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t byte = (w4[g] >> (8 * b)) & 0xFFu;
-        const float2 cc = lut32_l[byte * 16];
-        const uint32_t wv = nf4_pair_multirow(cc.x, cc.y, absmax);
-#pragma unroll
-        for (int t = 0; t < kMaxTok; ++t) {
-          if (t < n) {
-            const uint32_t xw = (b == 0) ? xv[t].x : (b == 1) ? xv[t].y : (b == 2) ? xv[t].z : xv[t].w;
-            acc[t] = fma_f16f16_f32(lo16(xw), lo16(wv), acc[t]);
-            acc[t] = fma_f16f16_f32(hi16(xw), hi16(wv), acc[t]);
-          }
-        }
-      }
-    }
-  }
-}
-
-// Shared prologue: per-expert counts, the active-expert list and the LUTs.
-struct ActiveSet {
-  int n_active;
+struct Active {
+  int n;
   int first;
-  bool any1, anyN;
 };
 
-__device__ __forceinline__ ActiveSet load_active(const DecodeArgs& a, int* s_off, int* s_active) {
+// Experts this launch serves: 1-token experts (!kMulti) or 2..8-token experts.
+template <bool kMulti>
+__device__ __forceinline__ Active load_active(const DecodeArgs& a, int* s_off, int* s_active) {
   __shared__ int s_n;
-  __shared__ int s_flags;
   if (threadIdx.x == 0) {
-    int n = 0, flags = 0;
+    int n = 0;
     for (int e = 0; e <= a.E; ++e) s_off[e] = a.expert_offsets[e];
     for (int e = 0; e < a.E; ++e) {
       const int cnt = s_off[e + 1] - s_off[e];
-      if (cnt > 0) {
-        s_active[n++] = e;
-        flags |= (cnt == 1) ? 1 : 2;
-      }
+      if (kMulti ? (cnt > 1 && cnt <= kMaxTok) : (cnt == 1)) s_active[n++] = e;
     }
     s_n = n;
-    s_flags = flags;
   }
   __syncthreads();
-  ActiveSet r;
-  r.n_active = s_n;
-  r.first = s_n > 0 ? s_active[0] : 0;
-  r.any1 = (s_flags & 1) != 0;
-  r.anyN = (s_flags & 2) != 0;
-  return r;
+  return Active{s_n, s_n > 0 ? s_active[0] : 0};
 }
 
-__global__ void __launch_bounds__(kThreads) k_gate_up_decode(const __grid_constant__ DecodeArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  uint32_t* lut16 = reinterpret_cast<uint32_t*>(smem);
-  float2* lut32 = reinterpret_cast<float2*>(smem + kLut16Words * 4);
-  uint4* xs = reinterpret_cast<uint4*>(smem + kLut16Words * 4 + kLut32Pairs * 8);
-  __shared__ int s_off[MOE_MAX_EXPERTS + 1];
-  __shared__ int s_active[MOE_MAX_EXPERTS];
-
-  const ActiveSet act = load_active(a, s_off, s_active);
-  if (act.n_active == 0) return;
-  build_luts(a.ex.e[act.first].w1.code, act.any1, act.anyN, lut16, lut32);
-
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t* lut16_l = lut16 + lane;
-  const float2* lut32_l = lut32 + (lane & 15);
-  const int items_per_expert = a.I / kRowsPerItem;
-  const int total = act.n_active * items_per_expert;
-  const int nchunks = a.H / 32;  // 16-byte chunks per row
-  const int xs_stride = nchunks * 4;
-  int staged = -1;
-
-  for (int item = blockIdx.x; item < total; item += gridDim.x) {
-    const int e = s_active[item / items_per_expert];
-    const int rb = item % items_per_expert;
-    const int base = s_off[e];
-    const int n = s_off[e + 1] - base;
-    if (e != staged) {
-      __syncthreads();
-      for (int i = threadIdx.x; i < n * nchunks * 4; i += kThreads) {
-        const int t = i / (nchunks * 4), rem = i - t * nchunks * 4;
-        const int c = rem >> 2, g = rem & 3;
-        const int64_t row = a.pair_token ? a.pair_token[base + t] : (int64_t)(base + t);
-        xs[t * xs_stride + xs_index(c, g)] =
-            reinterpret_cast<const uint4*>(a.x + row * a.H)[c * 4 + g];
-      }
-      __syncthreads();
-      staged = e;
+// x words of this thread for blocks [blk0, blk0+NBW): elements blk*64+16t..+16
+// of the token its B column carries (zeros past the expert's token count).
+template <int NBW>
+__device__ __forceinline__ void load_x(const uint16_t* row, bool valid, int blk0, int blk_end,
+                                       int lane, uint32_t (*xr)[8]) {
+  const int t = lane & 3;
+#pragma unroll
+  for (int kb = 0; kb < NBW; ++kb) {
+    uint4 u0 = make_uint4(0, 0, 0, 0), u1 = u0;
+    if (valid && blk0 + kb < blk_end) {
+      const uint4* p = reinterpret_cast<const uint4*>(row + (blk0 + kb) * 64 + 16 * t);
+      u0 = p[0];
+      u1 = p[1];
     }
-    const moe_nf4_matrix_t w1 = a.ex.e[e].w1, w3 = a.ex.e[e].w3;
-    const int64_t row_bytes = a.H / 2;
-    for (int rr = warp; rr < kRowsPerItem; rr += kWarps) {
-      const int r = rb * kRowsPerItem + rr;
-      float acc1[kMaxTok], acc3[kMaxTok];
+    xr[kb][0] = u0.x; xr[kb][1] = u0.y; xr[kb][2] = u0.z; xr[kb][3] = u0.w;
+    xr[kb][4] = u1.x; xr[kb][5] = u1.y; xr[kb][6] = u1.z; xr[kb][7] = u1.w;
+  }
+}
+
+// Items per reduction batch: one barrier per batch; partials of two batches
+// live in the dynamic shared memory below the table window.
+template <bool kMulti>
+constexpr int batch_items() { return kMulti ? 2 : 4; }
+template <bool kMulti>
+constexpr int red_cols() { return kMulti ? kMaxTok : 1; }
+template <bool kMulti>
+constexpr int red_floats() { return 2 * batch_items<kMulti>() * kWarpsK * 16 * red_cols<kMulti>(); }
+
+// Register-resident loads of one item (this warp's K part, rows g and g+8).
+template <int NBW>
+struct ItemLoads {
+  uint2 qa[NBW], qb[NBW];
+  float sa[NBW], sb[NBW];
+};
+
+// Loads of MMA rows A (tile row ra) and B (tile row rb_) of matrices ma / mb,
+// blocks [blk0, blk0+NBW) of tile rb, skipping blocks >= blk_end.
+template <int NBW>
+__device__ __forceinline__ void load_item(ItemLoads<NBW>& L, const moe_nf4_matrix_t& ma, int ra,
+                                          const moe_nf4_matrix_t& mb, int rb_, int rb, int nblk,
+                                          int blk0, int blk_end, int t) {
 #pragma unroll
-      for (int t = 0; t < kMaxTok; ++t) acc1[t] = acc3[t] = 0.0f;
-      const uint4* q1 = reinterpret_cast<const uint4*>(w1.q + r * row_bytes);
-      const uint4* q3 = reinterpret_cast<const uint4*>(w3.q + r * row_bytes);
-      const float* am1 = w1.absmax + (int64_t)r * (a.H / 64);
-      const float* am3 = w3.absmax + (int64_t)r * (a.H / 64);
-      for (int c = lane; c < nchunks; c += 32) {
-        const uint4 v1 = __ldg(q1 + c), v3 = __ldg(q3 + c);
-        const float s1 = __ldg(am1 + (c >> 1)), s3 = __ldg(am3 + (c >> 1));
-        if (n == 1) {
-          chunk_dot<true>(v1, s1, lut16_l, lut32_l, xs, xs_stride, c, 1, acc1);
-          chunk_dot<true>(v3, s3, lut16_l, lut32_l, xs, xs_stride, c, 1, acc3);
-        } else {
-          chunk_dot<false>(v1, s1, lut16_l, lut32_l, xs, xs_stride, c, n, acc1);
-          chunk_dot<false>(v3, s3, lut16_l, lut32_l, xs, xs_stride, c, n, acc3);
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < kMaxTok; ++t) {
-        if (t < n) {
-          const float g = warp_sum(acc1[t]);
-          const float u = warp_sum(acc3[t]);
-          if (lane == 0) a.h_sorted[(int64_t)(base + t) * a.I + r] = swiglu_f16(f2h(g), f2h(u));
-        }
-      }
+  for (int kb = 0; kb < NBW; ++kb) {
+    L.qa[kb] = L.qb[kb] = make_uint2(0x77777777u, 0x77777777u);  // NF4 code 7 == 0.0
+    L.sa[kb] = L.sb[kb] = 0.f;
+    if (blk0 + kb < blk_end) {
+      const int64_t seg = ((int64_t)rb * nblk + blk0 + kb) * 16;
+      L.qa[kb] = ldg_stream64(ma.q + (seg + ra) * 32 + t * 8);
+      L.qb[kb] = ldg_stream64(mb.q + (seg + rb_) * 32 + t * 8);
+      L.sa[kb] = __ldg(ma.absmax + seg + ra);
+      L.sb[kb] = __ldg(mb.absmax + seg + rb_);
     }
   }
 }
 
-__global__ void __launch_bounds__(kThreads) k_down_decode(const __grid_constant__ DecodeArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  uint32_t* lut16 = reinterpret_cast<uint32_t*>(smem);
-  float2* lut32 = reinterpret_cast<float2*>(smem + kLut16Words * 4);
-  uint4* xs = reinterpret_cast<uint4*>(smem + kLut16Words * 4 + kLut32Pairs * 8);
+// acc[0..1] = MMA row A (columns 2t, 2t+1), acc[2..3] = MMA row B.
+template <int NBW, bool kMulti>
+__device__ __forceinline__ void compute_item(const ItemLoads<NBW>& L, const uint32_t (*xr)[8],
+                                             uint32_t base, float* acc) {
+  acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+#pragma unroll
+  for (int kb = 0; kb < NBW; ++kb) {
+    if (kMulti) {
+      block_mma<true>(L.qa[kb], L.qb[kb], L.sa[kb], L.sb[kb], xr[kb], base, acc);
+    } else {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      block_mma<false>(L.qa[kb], L.qb[kb], 0.f, 0.f, xr[kb], base, d);
+      acc[0] = fmaf(L.sa[kb], d[0], acc[0]);
+      acc[2] = fmaf(L.sb[kb], d[2], acc[2]);
+    }
+  }
+}
+
+template <bool kMulti>
+__device__ __forceinline__ void stash(float* red, int slot, int warp, int g, int t, const float* acc) {
+  constexpr int C = red_cols<kMulti>();
+  float* p = red + ((slot * kWarpsK + warp) * 16) * C;
+  if (kMulti) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      p[g * C + 2 * t + c] = acc[c];
+      p[(g + 8) * C + 2 * t + c] = acc[2 + c];
+    }
+  } else if (t == 0) {
+    p[g] = acc[0];
+    p[g + 8] = acc[2];
+  }
+}
+
+// Sum of the 16 warp partials (warp order) of (slot, row, column).
+template <bool kMulti>
+__device__ __forceinline__ float reduce_partials(const float* red, int slot, int row, int col) {
+  constexpr int C = red_cols<kMulti>();
+  const float* p = red + (slot * kWarpsK * 16 + row) * C + col;
+  float s = p[0];
+#pragma unroll
+  for (int w = 1; w < kWarpsK; ++w) s = __fadd_rn(s, p[w * 16 * C]);
+  return s;
+}
+
+// gate_up.  NBW = 64-element blocks per warp (16 warps split H).  Item = 8 rows
+// of W1 and the same 8 rows of W3 (one MMA).
+template <int NBW, bool kMulti>
+__global__ void __launch_bounds__(kThreadsK, 1) k_gate_up_mma(const __grid_constant__ DecodeArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_off[MOE_MAX_EXPERTS + 1];
   __shared__ int s_active[MOE_MAX_EXPERTS];
+  constexpr int B = batch_items<kMulti>();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  Active act;
+  float* red = nullptr;
+  {
+    act = load_active<kMulti>(a, s_off, s_active);
+    if (act.n == 0) return;
+    if (smem_u32(smem) + red_floats<kMulti>() * 4 > kLutWin) return;
+    if (!build_lut(a.ex.e[act.first].w1.code, smem)) return;
+    red = reinterpret_cast<float*>(smem);
+  }
+  const int H = a.H, I = a.I;
+  const int nblk = H / 64;
+  const int items_per_expert = I / 8;  // half tiles of 8 rows
+  const int total = act.n * items_per_expert;
+  int first, last;
+  cta_range(total, &first, &last);
+  const int my_items = last - first;
+  const uint32_t base = kMulti ? (kLutWin | 128u | ((lane & 15) * 8)) : (kLutWin | (lane * 4));
+  const int blk0 = warp * NBW;
+  int staged = -1;
+  uint32_t xr[NBW][8];
+  ItemLoads<NBW> cur, nxt;
 
-  const ActiveSet act = load_active(a, s_off, s_active);
-  if (act.n_active == 0) return;
-  build_luts(a.ex.e[act.first].w2.code, act.any1, act.anyN, lut16, lut32);
-
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t* lut16_l = lut16 + lane;
-  const float2* lut32_l = lut32 + (lane & 15);
-  const int row_blocks = a.H / kRowsPerItem;
-  const int items_per_expert = a.S * row_blocks;
-  const int total = act.n_active * items_per_expert;
-  const int nchunks = a.I / 32;
-  const int sc = a.split_chunks;
-  const int xs_stride = sc * 4;
-  int staged_e = -1, staged_s = -1;
-
-  for (int item = blockIdx.x; item < total; item += gridDim.x) {
+  auto item_of = [&](int i) { return first + i; };
+  // One thread pulls the whole 16-row tile (W1, W3, both absmax) of an upcoming
+  // item into L2 when that item starts a tile (or starts this CTA's range).
+  auto prefetch = [&](int i) {
+    if (threadIdx.x != 0 || i >= my_items) return;
+    const int item = item_of(i);
+    const int hi = item % items_per_expert;
+    if ((hi & 1) && i != 0) return;
+    const moe_nf4_expert_t& ex = a.ex.e[s_active[item / items_per_expert]];
+    const int64_t tile = hi >> 1;
+    const uint32_t qbytes = 16u * (H / 2), abytes = 16u * (H / 64) * 4u;
+    prefetch_l2(ex.w1.q + tile * qbytes, qbytes);
+    prefetch_l2(ex.w3.q + tile * qbytes, qbytes);
+    prefetch_l2(ex.w1.absmax + tile * (abytes / 4), abytes);
+    prefetch_l2(ex.w3.absmax + tile * (abytes / 4), abytes);
+  };
+  for (int i = 0; i < kPrefetchItems && i < my_items; ++i) prefetch(i);
+  auto issue = [&](ItemLoads<NBW>& L, int i) {
+    const int item = item_of(i);
+    const moe_nf4_expert_t& ex = a.ex.e[s_active[item / items_per_expert]];
+    const int hi = item % items_per_expert;
+    const int rsub = (hi & 1) * 8 + g;
+    load_item<NBW>(L, ex.w1, rsub, ex.w3, rsub, hi >> 1, nblk, blk0, nblk, t);
+  };
+  if (my_items > 0) issue(cur, 0);
+  for (int i = 0; i < my_items; ++i) {
+    prefetch(i + kPrefetchItems);
+    if (i + 1 < my_items) issue(nxt, i + 1);
+    const int item = item_of(i);
     const int e = s_active[item / items_per_expert];
-    const int rem_item = item % items_per_expert;
-    const int s = rem_item / row_blocks;
-    const int rb = rem_item % row_blocks;
-    const int base = s_off[e];
-    const int n = s_off[e + 1] - base;
-    const int c0 = s * sc;
-    const int c1 = min(c0 + sc, nchunks);
-    if (e != staged_e || s != staged_s) {
+    const int tok0 = s_off[e];
+    const int n = s_off[e + 1] - tok0;
+    if (e != staged) {
+      const int tok = kMulti ? g : 0;
+      const bool valid = tok < n;
+      const int64_t xrow =
+          valid ? (a.pair_token ? a.pair_token[tok0 + tok] : (int64_t)(tok0 + tok)) : 0;
+      load_x<NBW>(a.x + xrow * H, valid, blk0, nblk, lane, xr);
+      staged = e;
+    }
+    float acc[4];
+    compute_item<NBW, kMulti>(cur, xr, base, acc);
+    const int slot = (i / B) % 2 * B + i % B;
+    stash<kMulti>(red, slot, warp, g, t, acc);
+    if (i % B == B - 1 || i == my_items - 1) {
       __syncthreads();
-      const int span = (c1 - c0) * 4;
-      for (int i = threadIdx.x; i < n * span; i += kThreads) {
-        const int t = i / span, rem = i - t * span;
-        const int cl = rem >> 2, g = rem & 3;
-        xs[t * xs_stride + xs_index(cl, g)] =
-            reinterpret_cast<const uint4*>(a.h_sorted + (int64_t)(base + t) * a.I)[(c0 + cl) * 4 + g];
+      // Finalize the batch: items i0..i of this batch, 8 rows x tokens each.
+      const int i0 = i - i % B;
+      const int nb = i - i0 + 1;
+      for (int job = threadIdx.x; job < nb * 8 * kMaxTok; job += blockDim.x) {
+        const int bi = job / (8 * kMaxTok), rem = job % (8 * kMaxTok);
+        const int rr = rem & 7, tok = rem >> 3;
+        const int it2 = item_of(i0 + bi);
+        const int e2 = s_active[it2 / items_per_expert];
+        const int t0 = s_off[e2], n2 = s_off[e2 + 1] - t0;
+        if (tok >= (kMulti ? n2 : 1)) continue;
+        const int sl = ((i0 + bi) / B) % 2 * B + bi;
+        const float gs = reduce_partials<kMulti>(red, sl, rr, kMulti ? tok : 0);
+        const float us = reduce_partials<kMulti>(red, sl, rr + 8, kMulti ? tok : 0);
+        const int hi = it2 % items_per_expert;
+        const int r = (hi >> 1) * 16 + (hi & 1) * 8 + rr;
+        a.h_sorted[(int64_t)(t0 + tok) * I + r] = swiglu_f16(f2h(gs), f2h(us));
       }
-      __syncthreads();
+    }
+    cur = nxt;
+  }
+}
+
+// down.  NBW = 64-element blocks per warp of one 2048-element split.  Item =
+// (split s, tile of 16 W2 rows).
+template <int NBW, bool kMulti>
+__global__ void __launch_bounds__(kThreadsK, 1) k_down_mma(const __grid_constant__ DecodeArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_off[MOE_MAX_EXPERTS + 1];
+  __shared__ int s_active[MOE_MAX_EXPERTS];
+  constexpr int B = batch_items<kMulti>();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  Active act;
+  float* red = nullptr;
+  {
+    act = load_active<kMulti>(a, s_off, s_active);
+    if (act.n == 0) return;
+    if (smem_u32(smem) + red_floats<kMulti>() * 4 > kLutWin) return;
+    if (!build_lut(a.ex.e[act.first].w2.code, smem)) return;
+    red = reinterpret_cast<float*>(smem);
+  }
+  const int H = a.H, I = a.I;
+  const int nblk = I / 64;
+  const int tiles = H / 16;
+  const int items_per_expert = a.S * tiles;
+  const int total = act.n * items_per_expert;
+  int first, last;
+  cta_range(total, &first, &last);
+  const int my_items = last - first;
+  const uint32_t base = kMulti ? (kLutWin | 128u | ((lane & 15) * 8)) : (kLutWin | (lane * 4));
+  int staged_e = -1, staged_s = -1;
+  uint32_t xr[NBW][8];
+  ItemLoads<NBW> cur, nxt;
+
+  auto item_of = [&](int i) { return first + i; };
+  // One thread pulls an upcoming item's blocks (contiguous in tile16) into L2.
+  auto prefetch = [&](int i) {
+    if (threadIdx.x != 0 || i >= my_items) return;
+    const int item = item_of(i);
+    const moe_nf4_expert_t& ex = a.ex.e[s_active[item / items_per_expert]];
+    const int rem = item % items_per_expert;
+    const int s = rem / tiles, rb = rem % tiles;
+    const int b0 = s * (kDownSlice / 64), b1 = min(b0 + kDownSlice / 64, nblk);
+    const int64_t seg0 = ((int64_t)rb * nblk + b0) * 16;
+    prefetch_l2(ex.w2.q + seg0 * 32, (uint32_t)(b1 - b0) * 512u);
+    prefetch_l2(ex.w2.absmax + seg0, (uint32_t)(b1 - b0) * 64u);
+  };
+  for (int i = 0; i < kPrefetchItems && i < my_items; ++i) prefetch(i);
+  auto issue = [&](ItemLoads<NBW>& L, int i) {
+    const int item = item_of(i);
+    const moe_nf4_expert_t& ex = a.ex.e[s_active[item / items_per_expert]];
+    const int rem = item % items_per_expert;
+    const int s = rem / tiles, rb = rem % tiles;
+    const int b0 = s * (kDownSlice / 64) + warp * NBW;
+    const int bend = min((s + 1) * (kDownSlice / 64), nblk);
+    load_item<NBW>(L, ex.w2, g, ex.w2, g + 8, rb, nblk, b0, bend, t);
+  };
+  if (my_items > 0) issue(cur, 0);
+  for (int i = 0; i < my_items; ++i) {
+    prefetch(i + kPrefetchItems);
+    if (i + 1 < my_items) issue(nxt, i + 1);
+    const int item = item_of(i);
+    const int e = s_active[item / items_per_expert];
+    const int rem = item % items_per_expert;
+    const int s = rem / tiles;
+    const int tok0 = s_off[e];
+    const int n = s_off[e + 1] - tok0;
+    if (e != staged_e || s != staged_s) {
+      const int blk0 = s * (kDownSlice / 64) + warp * NBW;
+      const int blk_end = min((s + 1) * (kDownSlice / 64), nblk);
+      const int tok = kMulti ? g : 0;
+      const bool valid = tok < n;
+      load_x<NBW>(a.h_sorted + (int64_t)(tok0 + (valid ? tok : 0)) * I, valid, blk0, blk_end,
+                  lane, xr);
       staged_e = e;
       staged_s = s;
     }
-    const moe_nf4_matrix_t w2 = a.ex.e[e].w2;
-    const int64_t row_bytes = a.I / 2;
-    for (int rr = warp; rr < kRowsPerItem; rr += kWarps) {
-      const int r = rb * kRowsPerItem + rr;
-      float acc[kMaxTok];
-#pragma unroll
-      for (int t = 0; t < kMaxTok; ++t) acc[t] = 0.0f;
-      const uint4* q = reinterpret_cast<const uint4*>(w2.q + r * row_bytes);
-      const float* am = w2.absmax + (int64_t)r * (a.I / 64);
-      for (int c = c0 + lane; c < c1; c += 32) {
-        const uint4 v = __ldg(q + c);
-        const float sa = __ldg(am + (c >> 1));
-        if (n == 1)
-          chunk_dot<true>(v, sa, lut16_l, lut32_l, xs, xs_stride, c - c0, 1, acc);
-        else
-          chunk_dot<false>(v, sa, lut16_l, lut32_l, xs, xs_stride, c - c0, n, acc);
-      }
-#pragma unroll
-      for (int t = 0; t < kMaxTok; ++t) {
-        if (t < n) {
-          const float y = warp_sum(acc[t]);
-          if (lane == 0) a.y_part[((int64_t)(base + t) * a.S + s) * a.H + r] = y;
-        }
+    float acc[4];
+    compute_item<NBW, kMulti>(cur, xr, base, acc);
+    const int slot = (i / B) % 2 * B + i % B;
+    stash<kMulti>(red, slot, warp, g, t, acc);
+    if (i % B == B - 1 || i == my_items - 1) {
+      __syncthreads();
+      const int i0 = i - i % B;
+      const int nb = i - i0 + 1;
+      for (int job = threadIdx.x; job < nb * 16 * kMaxTok; job += blockDim.x) {
+        const int bi = job / (16 * kMaxTok), rem2 = job % (16 * kMaxTok);
+        const int rr = rem2 & 15, tok = rem2 >> 4;
+        const int it2 = item_of(i0 + bi);
+        const int e2 = s_active[it2 / items_per_expert];
+        const int t0 = s_off[e2], n2 = s_off[e2 + 1] - t0;
+        if (tok >= (kMulti ? n2 : 1)) continue;
+        const int sl = ((i0 + bi) / B) % 2 * B + bi;
+        const float ys = reduce_partials<kMulti>(red, sl, rr, kMulti ? tok : 0);
+        const int r2 = it2 % items_per_expert;
+        const int s2 = r2 / tiles, rb2 = r2 % tiles;
+        a.y_part[((int64_t)(t0 + tok) * a.S + s2) * H + rb2 * 16 + rr] = ys;
       }
     }
+    cur = nxt;
   }
 }
 
@@ -322,35 +493,67 @@ __global__ void k_identity_offsets(int32_t* off, int n) {
   }
 }
 
+template <class K>
+bool smem_attr(K kernel) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem) ==
+         cudaSuccess;
+}
+
+template <bool kMulti>
+bool attrs() {
+  return smem_attr(k_gate_up_mma<1, kMulti>) && smem_attr(k_gate_up_mma<2, kMulti>) &&
+         smem_attr(k_gate_up_mma<4, kMulti>) && smem_attr(k_gate_up_mma<8, kMulti>) &&
+         smem_attr(k_down_mma<kDownSlice / (64 * kWarpsK), kMulti>);
+}
+
+// Blocks per K part of the gate_up kernels: ceil(H / 64 / 16) rounded up to
+// a power of two (parts past the row are idle).
+int gate_nbw(int hidden) {
+  const int need = static_cast<int>(ceil_div(hidden / 64, kWarpsK));
+  return need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : -1;
+}
+
+template <bool kMulti>
+int launch_gate(const DecodeArgs& a, cudaStream_t s) {
+  const int grid = sm_count();
+  switch (gate_nbw(a.H)) {
+    case 1: k_gate_up_mma<1, kMulti><<<grid, kThreadsK, kDynSmem, s>>>(a); break;
+    case 2: k_gate_up_mma<2, kMulti><<<grid, kThreadsK, kDynSmem, s>>>(a); break;
+    case 4: k_gate_up_mma<4, kMulti><<<grid, kThreadsK, kDynSmem, s>>>(a); break;
+    case 8: k_gate_up_mma<8, kMulti><<<grid, kThreadsK, kDynSmem, s>>>(a); break;
+    default: return MOE_ERR_UNSUPPORTED;
+  }
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
+template <bool kMulti>
+int launch_down(const DecodeArgs& a, cudaStream_t s) {
+  k_down_mma<kDownSlice / (64 * kWarpsK), kMulti><<<sm_count(), kThreadsK, kDynSmem, s>>>(a);
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
 }  // namespace
 
-// Choose the K-split of the W2 reduction: splits of `split_chunks` 16-byte
-// chunks, a multiple of 32 (one per lane) where the row allows.
-void decode_split(int inter, int* S, int* split_chunks) {
-  const int nchunks = inter / 32;
-  int sc = 64;  // 2 chunks per lane
-  if (nchunks <= sc) sc = nchunks;
-  *split_chunks = sc;
-  *S = static_cast<int>(ceil_div(nchunks, sc));
+// Shapes the decode kernels accept: H and I multiples of 64 (one absmax block)
+// with H up to 8192.
+bool decode_supported(int hidden, int inter) {
+  return hidden > 0 && inter > 0 && hidden % 64 == 0 && inter % 64 == 0 && gate_nbw(hidden) > 0;
 }
 
-size_t decode_smem_bytes(int hidden, int inter, int split_chunks) {
-  const size_t lut = (size_t)kLut16Words * 4 + (size_t)kLut32Pairs * 8;
-  const size_t xs_gate = (size_t)kMaxTok * hidden * 2;
-  const size_t xs_down = (size_t)kMaxTok * split_chunks * 64;
-  (void)inter;
-  return lut + (xs_gate > xs_down ? xs_gate : xs_down);
-}
-
+// Down-projection K splits of 2048 elements (the last may be partial).
+int decode_splits(int inter) { return static_cast<int>(ceil_div(inter, kDownSlice)); }
 int decode_max_tokens() { return kMaxTok; }
 
 int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t* expert_offsets,
                           const int32_t* pair_token, const uint16_t* x, int hidden, int inter,
-                          uint16_t* h_sorted, float* y_part, int S, int split_chunks,
+                          uint16_t* h_sorted, float* y_part, int max_tokens_per_expert,
                           cudaStream_t s) {
   if (E < 1 || E > MOE_MAX_EXPERTS) return MOE_ERR_INVALID_ARG;
-  if (hidden % kRowsPerItem || inter % kRowsPerItem || hidden % 32 || inter % 32)
-    return MOE_ERR_UNSUPPORTED;
+  if (!decode_supported(hidden, inter)) return MOE_ERR_UNSUPPORTED;
+  static bool attr_ok = attrs<false>() && attrs<true>();
+  if (!attr_ok) return MOE_ERR_CUDA;
   DecodeArgs a{};
   for (int e = 0; e < E; ++e) a.ex.e[e] = experts[e];
   a.E = E;
@@ -361,24 +564,13 @@ int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t*
   a.y_part = y_part;
   a.H = hidden;
   a.I = inter;
-  a.S = S;
-  a.split_chunks = split_chunks;
-  const size_t smem = decode_smem_bytes(hidden, inter, split_chunks);
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaFuncSetAttribute(k_gate_up_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    cudaFuncSetAttribute(k_down_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    attr_done = true;
-  }
-  if (smem > 160 * 1024) return MOE_ERR_UNSUPPORTED;
-  const int grid_cap = sm_count() * 2;
-  const int gate_items = E * (inter / kRowsPerItem);
-  const int down_items = E * S * (hidden / kRowsPerItem);
-  k_gate_up_decode<<<gate_items < grid_cap ? gate_items : grid_cap, kThreads, smem, s>>>(a);
-  MOE_CHECK_LAUNCH();
-  k_down_decode<<<down_items < grid_cap ? down_items : grid_cap, kThreads, smem, s>>>(a);
-  MOE_CHECK_LAUNCH();
-  return MOE_OK;
+  a.S = decode_splits(inter);
+  const bool multi = max_tokens_per_expert > 1;
+  int st = launch_gate<false>(a, s);
+  if (st == MOE_OK && multi) st = launch_gate<true>(a, s);
+  if (st == MOE_OK) st = launch_down<false>(a, s);
+  if (st == MOE_OK && multi) st = launch_down<true>(a, s);
+  return st;
 }
 
 int launch_reduce_partials(const float* part, int64_t P, int S, int width, uint16_t* y,

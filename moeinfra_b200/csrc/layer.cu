@@ -11,11 +11,12 @@
 namespace moe {
 
 // expert_decode.cu
-void decode_split(int inter, int* S, int* split_chunks);
+bool decode_supported(int hidden, int inter);
+int decode_splits(int inter);
 int decode_max_tokens();
 int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t* expert_offsets,
                           const int32_t* pair_token, const uint16_t* x, int hidden, int inter,
-                          uint16_t* h_sorted, float* y_part, int S, int split_chunks,
+                          uint16_t* h_sorted, float* y_part, int max_tokens_per_expert,
                           cudaStream_t s);
 int launch_reduce_partials(const float* part, int64_t P, int S, int width, uint16_t* y,
                            cudaStream_t s);
@@ -73,9 +74,7 @@ size_t carve_layer(unsigned char* ws, int64_t T, int hidden, int inter, int E, i
   b->pair_slot = c.take<int32_t>(P);
   b->h_sorted = c.take<uint16_t>((size_t)P * inter);
   if (use_decode_path(T)) {
-    int S, sc;
-    decode_split(inter, &S, &sc);
-    b->y_part = c.take<float>((size_t)P * S * hidden);
+    b->y_part = c.take<float>((size_t)P * decode_splits(inter) * hidden);
     b->x_sorted = b->y_sorted = nullptr;
   } else {
     b->y_part = nullptr;
@@ -85,16 +84,14 @@ size_t carve_layer(unsigned char* ws, int64_t T, int hidden, int inter, int E, i
   return c.used;
 }
 
-bool shapes_ok(int hidden, int inter) {
-  return hidden > 0 && inter > 0 && hidden % 128 == 0 && inter % 128 == 0;
-}
+bool shapes_ok(int hidden, int inter) { return decode_supported(hidden, inter); }
 
 bool experts_aligned(const moe_nf4_expert_t* ex, int E) {
   for (int e = 0; e < E; ++e) {
     const moe_nf4_matrix_t* m[3] = {&ex[e].w1, &ex[e].w3, &ex[e].w2};
     for (auto* mm : m) {
       if (!mm->q || !mm->absmax || !mm->code) return false;
-      if (!aligned16(mm->q)) return false;
+      if (!aligned16(mm->q) || (reinterpret_cast<uintptr_t>(mm->absmax) & 3)) return false;
     }
   }
   return true;
@@ -131,13 +128,11 @@ extern "C" int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
   if (st != MOE_OK) return st;
   const int64_t P = T * k;
   if (use_decode_path(T)) {
-    int S, sc;
-    decode_split(inter, &S, &sc);
     st = launch_decode_experts(experts, E, b.offsets, b.pair_token, h, hidden, inter, b.h_sorted,
-                               b.y_part, S, sc, s);
+                               b.y_part, static_cast<int>(T), s);
     if (st != MOE_OK) return st;
-    return launch_combine_partials(b.y_part, S, b.pair_slot, indices, weights, T, k, hidden, out,
-                                   s);
+    return launch_combine_partials(b.y_part, decode_splits(inter), b.pair_slot, indices, weights,
+                                   T, k, hidden, out, s);
   }
   st = moe_gather_rows(h, b.pair_token, P, hidden, b.x_sorted, s);
   if (st != MOE_OK) return st;
@@ -159,9 +154,7 @@ size_t carve_expert(unsigned char* ws, int64_t n, int hidden, int inter, ExpertB
   b->offsets = c.take<int32_t>(2);
   b->h = c.take<uint16_t>((size_t)n * inter);
   if (use_decode_path(n)) {
-    int S, sc;
-    decode_split(inter, &S, &sc);
-    b->y_part = c.take<float>((size_t)n * S * hidden);
+    b->y_part = c.take<float>((size_t)n * decode_splits(inter) * hidden);
   } else {
     b->y_part = nullptr;
   }
@@ -193,12 +186,10 @@ extern "C" int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t
   int st = launch_identity_offsets(b.offsets, static_cast<int>(n), s);
   if (st != MOE_OK) return st;
   if (use_decode_path(n)) {
-    int S, sc;
-    decode_split(inter, &S, &sc);
-    st = launch_decode_experts(expert, 1, b.offsets, nullptr, x, hidden, inter, b.h, b.y_part, S,
-                               sc, s);
+    st = launch_decode_experts(expert, 1, b.offsets, nullptr, x, hidden, inter, b.h, b.y_part,
+                               static_cast<int>(n), s);
     if (st != MOE_OK) return st;
-    return launch_reduce_partials(b.y_part, n, S, hidden, y, s);
+    return launch_reduce_partials(b.y_part, n, decode_splits(inter), hidden, y, s);
   }
   return launch_grouped_gemm_experts(expert, 1, b.offsets, x, n, hidden, inter, b.h, y, s);
 }

@@ -6,8 +6,9 @@
 //   w, idx = topk(p, k)                                              (:86-90)
 //   w /= w.sum(-1, keepdim=True)                                     (:92)
 //
-// One warp per token.  Lane j (< E) owns expert j after the dot-product
-// reduction.  The softmax follows the operation order of torch's CUDA warp
+// Few tokens: one CTA per token (8 warps split H, so every load of the row is
+// in flight at once); many tokens: one warp per token.  Lane j (< E) owns
+// expert j after the dot-product reduction.  The softmax follows the operation order of torch's CUDA warp
 // softmax for a last dimension <= 32: butterfly max and butterfly sum over
 // next_pow2(E) lanes (offsets W/2 .. 1), exp(l - max), then e / sum, so the
 // fp32 probabilities are reproduced operation for operation.
@@ -21,8 +22,9 @@ constexpr int kRouterWarps = 8;
 __device__ __forceinline__ void topk_renorm(float p, int lane, int E, int W, int k, int64_t t,
                                             float* __restrict__ weights,
                                             int64_t* __restrict__ indices) {
-  // Iterative arg-max: larger probability wins; exact ties go to the lower
-  // expert index.  Lanes >= E never win (p = -1 sentinel; probabilities >= 0).
+  // Iterative arg-max: larger probability wins; among exact ties the lower
+  // expert index is selected first.  Lanes >= E never win (p = -1 sentinel;
+  // probabilities are >= 0).
   float cand = (lane < E) ? p : -1.0f;
   float sel_sum = 0.0f;
   float my_sel = -1.0f;  // selected probability held by output lane j
@@ -48,9 +50,24 @@ __device__ __forceinline__ void topk_renorm(float p, int lane, int E, int W, int
     }
     if (lane == bi) cand = -1.0f;
   }
+  // The selected set takes the lower expert indices among equal probabilities;
+  // torch's CUDA topk then lists equal values in descending index order.
+  // Reverse each run of equal selected values to match (runs are contiguous:
+  // the selection order is descending in value).
+  int rs = lane, re = lane;
+  for (int m = 0; m < k; ++m) {
+    const float vm = __shfl_sync(0xffffffffu, my_sel, m);
+    if (lane < k && vm == my_sel) {
+      rs = min(rs, m);
+      re = max(re, m);
+    }
+  }
+  const int src = (lane < k) ? rs + re - lane : lane;
+  const float out_sel = __shfl_sync(0xffffffffu, my_sel, src);
+  const int out_idx = __shfl_sync(0xffffffffu, my_idx, src);
   if (lane < k) {
-    weights[t * k + lane] = __fdiv_rn(my_sel, sel_sum);
-    indices[t * k + lane] = static_cast<int64_t>(my_idx);
+    weights[t * k + lane] = __fdiv_rn(out_sel, sel_sum);
+    indices[t * k + lane] = static_cast<int64_t>(out_idx);
   }
   (void)W;
 }
@@ -65,6 +82,80 @@ __device__ __forceinline__ float softmax_lane(float logit, int lane, int E, int 
   return __fdiv_rn(e, s);
 }
 
+// Dot products of one token against the E gate rows over the vector range
+// [v_begin, v_end) handled by this lane (stride `stride` vectors of 8 fp16).
+// Float-float accumulator: value = hi + lo, updated with the error-free
+// TwoSum, so a 4096-term sum of exact fp16 x fp16 products keeps ~48 bits.
+struct FF {
+  float hi, lo;
+};
+__device__ __forceinline__ void ff_add(FF& a, float p) {
+  const float s = __fadd_rn(a.hi, p);
+  const float bp = __fsub_rn(s, a.hi);
+  const float err = __fadd_rn(__fsub_rn(a.hi, __fsub_rn(s, bp)), __fsub_rn(p, bp));
+  a.hi = s;
+  a.lo = __fadd_rn(a.lo, err);
+}
+__device__ __forceinline__ void ff_merge(FF& a, const FF& b) {
+  ff_add(a, b.hi);
+  a.lo = __fadd_rn(a.lo, b.lo);
+}
+__device__ __forceinline__ double ff_value(const FF& a) { return (double)a.hi + (double)a.lo; }
+
+// fp16 x fp16 products are exact in fp32; they are summed in float-float and
+// rounded once to fp16, which gives the correctly rounded logit.
+template <int EMAX>
+__device__ __forceinline__ void gate_dots(const uint4* __restrict__ hrow, const uint4* __restrict__ wg,
+                                          int nvec, int E, int v_begin, int stride,
+                                          FF (&acc)[EMAX]) {
+#pragma unroll 1
+  for (int v = v_begin; v < nvec; v += stride) {
+    uint4 hv = hrow[v];
+    const __half2* hh = reinterpret_cast<const __half2*>(&hv);
+    float2 x0 = __half22float2(hh[0]), x1 = __half22float2(hh[1]);
+    float2 x2 = __half22float2(hh[2]), x3 = __half22float2(hh[3]);
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e) {
+      if (e < E) {
+        uint4 wv = __ldg(wg + (int64_t)e * nvec + v);
+        const __half2* ww = reinterpret_cast<const __half2*>(&wv);
+        float2 w0 = __half22float2(ww[0]), w1 = __half22float2(ww[1]);
+        float2 w2 = __half22float2(ww[2]), w3 = __half22float2(ww[3]);
+        FF a = acc[e];
+        ff_add(a, __fmul_rn(x0.x, w0.x)); ff_add(a, __fmul_rn(x0.y, w0.y));
+        ff_add(a, __fmul_rn(x1.x, w1.x)); ff_add(a, __fmul_rn(x1.y, w1.y));
+        ff_add(a, __fmul_rn(x2.x, w2.x)); ff_add(a, __fmul_rn(x2.y, w2.y));
+        ff_add(a, __fmul_rn(x3.x, w3.x)); ff_add(a, __fmul_rn(x3.y, w3.y));
+        acc[e] = a;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ FF warp_sum_ff(FF v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    FF w;
+    w.hi = __shfl_xor_sync(0xffffffffu, v.hi, o);
+    w.lo = __shfl_xor_sync(0xffffffffu, v.lo, o);
+    ff_merge(v, w);
+  }
+  return v;
+}
+
+__device__ __forceinline__ void finish_token(double logit, int lane, int E, int W, int k,
+                                             int64_t t, uint16_t* __restrict__ logits,
+                                             float* __restrict__ weights,
+                                             int64_t* __restrict__ indices) {
+  // Round once to fp16 (F.linear output dtype), then softmax on float(logit).
+  uint16_t l16 = __half_as_ushort(__double2half(logit));
+  if (logits != nullptr && lane < E) logits[t * E + lane] = l16;
+  float p = softmax_lane(h2f(l16), lane, E, W);
+  topk_renorm(p, lane, E, W, k, t, weights, indices);
+}
+
+// Many tokens: one warp per token.
+template <int EMAX>
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(
     const uint4* __restrict__ h, const uint4* __restrict__ wg, int64_t T, int H, int E, int W,
     int k, uint16_t* __restrict__ logits, float* __restrict__ weights,
@@ -73,44 +164,54 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(
   const int64_t t = blockIdx.x * (int64_t)kRouterWarps + (threadIdx.x >> 5);
   if (t >= T) return;
   const int nvec = H >> 3;  // 8 fp16 per 16-byte vector
-  float acc[32];
+  FF acc[EMAX];
 #pragma unroll
-  for (int e = 0; e < 32; ++e) acc[e] = 0.0f;
-  const uint4* hrow = h + t * nvec;
-  for (int v = lane; v < nvec; v += 32) {
-    uint4 hv = hrow[v];
-    const __half2* hh = reinterpret_cast<const __half2*>(&hv);
-    float2 x0 = __half22float2(hh[0]), x1 = __half22float2(hh[1]);
-    float2 x2 = __half22float2(hh[2]), x3 = __half22float2(hh[3]);
+  for (int e = 0; e < EMAX; ++e) acc[e] = FF{0.f, 0.f};
+  gate_dots<EMAX>(h + t * nvec, wg, nvec, E, lane, 32, acc);
+  double mine = 0.0;
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      if (e < E) {
-        uint4 wv = __ldg(wg + (int64_t)e * nvec + v);
-        const __half2* ww = reinterpret_cast<const __half2*>(&wv);
-        float2 w0 = __half22float2(ww[0]), w1 = __half22float2(ww[1]);
-        float2 w2 = __half22float2(ww[2]), w3 = __half22float2(ww[3]);
-        float a = acc[e];
-        a = fmaf(x0.x, w0.x, a); a = fmaf(x0.y, w0.y, a);
-        a = fmaf(x1.x, w1.x, a); a = fmaf(x1.y, w1.y, a);
-        a = fmaf(x2.x, w2.x, a); a = fmaf(x2.y, w2.y, a);
-        a = fmaf(x3.x, w3.x, a); a = fmaf(x3.y, w3.y, a);
-        acc[e] = a;
-      }
-    }
-  }
-  float mine = 0.0f;
-#pragma unroll
-  for (int e = 0; e < 32; ++e) {
+  for (int e = 0; e < EMAX; ++e) {
     if (e < E) {
-      float s = warp_sum(acc[e]);
-      if (lane == e) mine = s;
+      const FF s = warp_sum_ff(acc[e]);
+      if (lane == e) mine = ff_value(s);
     }
   }
-  // Round once to fp16 (F.linear output dtype), then softmax on float(logit).
-  uint16_t l16 = f2h(mine);
-  if (logits != nullptr && lane < E) logits[t * E + lane] = l16;
-  float p = softmax_lane(h2f(l16), lane, E, W);
-  topk_renorm(p, lane, E, W, k, t, weights, indices);
+  finish_token(mine, lane, E, W, k, t, logits, weights, indices);
+}
+
+// Few tokens: one CTA per token, the 8 warps split H; partial sums meet in
+// shared memory (fixed order) so every load of the row is in flight at once.
+template <int EMAX>
+__global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk_cta(
+    const uint4* __restrict__ h, const uint4* __restrict__ wg, int64_t T, int H, int E, int W,
+    int k, uint16_t* __restrict__ logits, float* __restrict__ weights,
+    int64_t* __restrict__ indices) {
+  __shared__ FF s_part[kRouterWarps][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t = blockIdx.x;
+  const int nvec = H >> 3;
+  FF acc[EMAX];
+#pragma unroll
+  for (int e = 0; e < EMAX; ++e) acc[e] = FF{0.f, 0.f};
+  gate_dots<EMAX>(h + t * nvec, wg, nvec, E, threadIdx.x, kRouterWarps * 32, acc);
+#pragma unroll
+  for (int e = 0; e < EMAX; ++e) {
+    if (e < E) {
+      const FF s = warp_sum_ff(acc[e]);
+      if (lane == e) s_part[warp][e] = s;
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    double mine = 0.0;
+    if (lane < E) {
+      FF tot = s_part[0][lane];
+#pragma unroll
+      for (int w = 1; w < kRouterWarps; ++w) ff_merge(tot, s_part[w][lane]);
+      mine = ff_value(tot);
+    }
+    finish_token(mine, lane, E, W, k, t, logits, weights, indices);
+  }
 }
 
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router_from_logits(
@@ -141,10 +242,23 @@ extern "C" int moe_router_topk(const uint16_t* h, const uint16_t* wg, int64_t T,
   if (T == 0) return MOE_OK;
   if (!h || !wg || !weights || !indices) return MOE_ERR_INVALID_ARG;
   if (!aligned16(h) || !aligned16(wg)) return MOE_ERR_ALIGNMENT;
-  int grid = static_cast<int>(ceil_div(T, kRouterWarps));
-  k_router_topk<<<grid, kRouterWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint4*>(h), reinterpret_cast<const uint4*>(wg), T, H, E,
-      next_pow2(E), k, logits, weights, indices);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint4* h4 = reinterpret_cast<const uint4*>(h);
+  const uint4* w4 = reinterpret_cast<const uint4*>(wg);
+  const int W = next_pow2(E);
+  // Code size matters (each token runs the unrolled body once): instantiate
+  // for the expert-count bound that covers E.
+  if (T <= 2 * sm_count()) {
+    const int grid = static_cast<int>(T);
+    if (E <= 8) k_router_topk_cta<8><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
+    else if (E <= 16) k_router_topk_cta<16><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
+    else k_router_topk_cta<32><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
+  } else {
+    const int grid = static_cast<int>(ceil_div(T, kRouterWarps));
+    if (E <= 8) k_router_topk<8><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
+    else if (E <= 16) k_router_topk<16><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
+    else k_router_topk<32><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
+  }
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }

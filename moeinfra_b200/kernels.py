@@ -74,6 +74,30 @@ def nf4_dequant(q: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, numel
     return out
 
 
+def nf4_tile16(q: torch.Tensor, absmax: torch.Tensor, rows: int, cols: int):
+    """Store layout -> tile16 device layout (exact permutation); returns (q_t, absmax_t)."""
+    dev = _need_cuda("nf4_tile16", q=q, absmax=absmax)
+    _need_dtype("nf4_tile16", q, torch.uint8, "q")
+    _need_dtype("nf4_tile16", absmax, torch.float32, "absmax")
+    if q.numel() * 2 != rows * cols or absmax.numel() * NF4_BLOCKSIZE != rows * cols:
+        raise ValueError("nf4_tile16: tensor sizes do not match rows x cols")
+    q_out = torch.empty_like(q.reshape(-1))
+    a_out = torch.empty_like(absmax.reshape(-1))
+    check(_native.lib().moe_nf4_tile16(_p(q), _p(absmax), rows, cols, _p(q_out), _p(a_out),
+                                       _stream(dev)), "moe_nf4_tile16")
+    return q_out, a_out
+
+
+def nf4_dequant_tile16(q: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, rows: int,
+                       cols: int) -> torch.Tensor:
+    """bf16 [rows, cols] of a tile16 matrix (bit-exact with the store-layout dequant)."""
+    dev = _need_cuda("nf4_dequant_tile16", q=q, absmax=absmax, code=code)
+    out = torch.empty(rows, cols, dtype=torch.bfloat16, device=dev)
+    check(_native.lib().moe_nf4_dequant_tile16(_p(q), _p(absmax), _p(code), rows, cols, _p(out),
+                                               _stream(dev)), "moe_nf4_dequant_tile16")
+    return out
+
+
 def nested_absmax(qabs: torch.Tensor, absmax2: torch.Tensor, code2: torch.Tensor,
                   offset: float, blocksize2: int = NESTED_BLOCKSIZE) -> torch.Tensor:
     dev = _need_cuda("nested_absmax", qabs=qabs, absmax2=absmax2, code2=code2)

@@ -3,9 +3,10 @@
 API of the reference's ``transfer/nf4_reconstruct.py`` (``ReconstructedNF4Expert``,
 ``:117-166``).  The reference wraps the device tensors in bitsandbytes
 ``Linear4bit`` shells and runs three library matmuls; here construction only
-records device pointers (plus a one-time exact rebuild of a double-quantized
-absmax, ``:17-38``) and ``forward`` is one call of the fused B200 SwiGLU
-expert kernel on the packed weights (``:152-155``).
+re-lays each projection out once into the tile16 device layout (16-row x
+64-element tiles contiguous, an exact permutation; a double-quantized absmax is
+first rebuilt exactly, ``:17-38``) and ``forward`` is one call of the fused
+B200 SwiGLU expert kernel on the packed weights (``:152-155``).
 """
 from __future__ import annotations
 
@@ -59,11 +60,15 @@ class GPUNF4Linear(nn.Module):
                 raise ValueError(f"absmax must be fp32 when not nested, got {absmax.dtype}")
         if absmax.numel() * _NF4_BLOCKSIZE != numel:
             raise ValueError("absmax length does not match the weight shape")
+        if out_features % 16 or in_features % 64:
+            raise ValueError("NF4 expert kernels need out_features % 16 == 0 and in_features % 64 == 0")
         self.in_features = in_features
         self.out_features = out_features
         self.compute_dtype = torch.float16
-        self.packed = weight.reshape(-1).contiguous()
-        self.absmax = absmax.reshape(-1).contiguous()
+        # tile16 device layout: every kernel reads 16-row x 64-element tiles.
+        self.packed, self.absmax = kernels.nf4_tile16(
+            weight.reshape(-1).contiguous(), absmax.reshape(-1).contiguous().float(),
+            out_features, in_features)
         self.code = code.reshape(-1).contiguous()
 
     @property
@@ -72,9 +77,8 @@ class GPUNF4Linear(nn.Module):
 
     def dequantize(self) -> torch.Tensor:
         """bf16 weight [out, in], bit-exact with bitsandbytes' dequantize_4bit."""
-        return kernels.nf4_dequant(self.packed, self.absmax, self.code,
-                                   self.in_features * self.out_features).view(
-            self.out_features, self.in_features)
+        return kernels.nf4_dequant_tile16(self.packed, self.absmax, self.code,
+                                          self.out_features, self.in_features)
 
     def descriptor(self):
         return kernels.matrix_desc(self.packed, self.absmax, self.code)

@@ -300,3 +300,16 @@ def make_expert(rng: np.random.Generator, hidden: int, inter: int,
                   "state2_absmax": a2, "state2_code": c2, "state2_offset": None}
         out[name] = st
     return out
+
+
+# ---------------------------------------------------------------------------
+# tile16 device layout (this build's resident layout; an exact permutation)
+# ---------------------------------------------------------------------------
+
+def tile16(q: np.ndarray, absmax: np.ndarray, rows: int, cols: int):
+    """Store layout -> tile16: (16-row tile, 64-element block, row, 32 bytes)."""
+    nblk = cols // 64
+    qb = np.asarray(q, np.uint8).reshape(rows // 16, 16, nblk, 32)
+    ab = np.asarray(absmax, np.float32).reshape(rows // 16, 16, nblk)
+    return (np.ascontiguousarray(qb.transpose(0, 2, 1, 3)).reshape(-1),
+            np.ascontiguousarray(ab.transpose(0, 2, 1)).reshape(-1))

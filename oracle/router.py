@@ -9,9 +9,11 @@ Restates ``ExpertRouter.route_with_logits`` (``engine/router.py:65-94``):
 2. ``softmax(logits.float(), -1)`` (``router.py:81-84``) in the operation
    order of torch's CUDA warp softmax for a last dim of 8: max, ``exp(l - max)``,
    a butterfly sum over lane offsets 4, 2, 1, then ``e / sum``.
-3. ``topk(p, k)`` (``router.py:86-90``): descending probability; exact ties
-   resolved toward the lower expert index (torch leaves tie order
-   unspecified; tests compare tied selections by value).
+3. ``topk(p, k)`` (``router.py:86-90``): descending probability.  Exact ties
+   follow torch's CUDA topk (the reference router runs on the GPU): the lower
+   expert indices are selected, and equal values are listed in descending
+   index order.  (torch's CPU topk differs on ties; tests compare tied
+   selections against CPU goldens by value.)
 4. ``w /= w.sum(-1)`` (``router.py:92``).
 """
 from __future__ import annotations
@@ -48,10 +50,15 @@ def softmax_f32(logits16: np.ndarray) -> np.ndarray:
     return (e / s).astype(np.float32)
 
 
-def topk_lower_index(p: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
-    """Top-k values/indices per row: descending value, ties -> lower index."""
-    order = np.lexsort((np.broadcast_to(np.arange(p.shape[-1]), p.shape), -p), axis=-1)[..., :k]
-    return np.take_along_axis(p, order, -1), order.astype(np.int64)
+def topk_cuda_order(p: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """Top-k per row: lower indices win ties for selection; output in
+    descending value, equal values in descending index."""
+    ar = np.broadcast_to(np.arange(p.shape[-1]), p.shape)
+    sel = np.lexsort((ar, -p), axis=-1)[..., :k]
+    vals = np.take_along_axis(p, sel, -1)
+    order = np.lexsort((-sel, -vals), axis=-1)
+    sel = np.take_along_axis(sel, order, -1)
+    return np.take_along_axis(p, sel, -1), sel.astype(np.int64)
 
 
 def route_with_logits(h16: np.ndarray, wg16: np.ndarray, k: int = 2):
@@ -62,7 +69,7 @@ def route_with_logits(h16: np.ndarray, wg16: np.ndarray, k: int = 2):
 
 def route_from_logits(lg16: np.ndarray, k: int = 2):
     p = softmax_f32(lg16)
-    w, idx = topk_lower_index(p, k)
+    w, idx = topk_cuda_order(p, k)
     s = w[..., 0].copy()
     for j in range(1, k):
         s = (s + w[..., j]).astype(np.float32)

@@ -142,3 +142,15 @@ def test_gemv_and_multirow_semantics_differ_by_bf16_rounding_only():
     b = onf4.dequant_weight_f16(st, (256, 128)).astype(np.float32)
     rel = np.abs(a - b) / np.maximum(np.abs(b), 1e-30)
     assert rel.max() < 2 ** -7
+
+
+def test_tile16_is_a_permutation_of_store_blocks():
+    rows, cols = 32, 128
+    q = np.arange(rows * cols // 2, dtype=np.int64).astype(np.uint8)
+    a = np.arange(rows * cols // 64, dtype=np.float32)
+    qt, at = onf4.tile16(q, a, rows, cols)
+    assert sorted(at.tolist()) == sorted(a.tolist())
+    # row 17, block 1 lives in tile 1, block 1, row 1
+    seg = ((1 * (cols // 64) + 1) * 16 + 1)
+    assert at[seg] == a[17 * (cols // 64) + 1]
+    assert np.array_equal(qt[seg * 32:(seg + 1) * 32], q[17 * cols // 2 + 32:17 * cols // 2 + 64])
