@@ -62,6 +62,12 @@ const char* moe_status_string(int status);
 /* Library build identifier (static storage). */
 const char* moe_version(void);
 
+/* Number of kernels this library has launched (or recorded into a stream
+ * capture) in this process, counted on the host at each launch.  A CUDA-graph
+ * replay re-runs the kernels captured without calling the library, so the
+ * count taken around a capture is the kernel count of one replay. */
+uint64_t moe_launch_count(void);
+
 /* Reads and clears the device-side error word that kernels set when one of
  * their bounded waits (bulk-copy pipeline barriers) times out.  Synchronous
  * (a device-to-host copy).  *value is 0 when no wait timed out. */
@@ -160,6 +166,19 @@ int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
                       void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Expert stage alone: SwiGLU experts on rows already grouped by expert (the
+ * rows of expert e are [expert_offsets[e], expert_offsets[e+1]) of x_sorted,
+ * device int32 [E+1]); y_sorted fp16 [P, hidden] in the same order.  Used after
+ * an expert-parallel dispatch and to time the expert kernels alone.  Same
+ * per-expert semantics as moe_expert_forward.
+ */
+size_t moe_experts_workspace_size(int64_t P, int hidden, int inter);
+int moe_experts_forward(const moe_nf4_expert_t* experts, int E,
+                        const int32_t* expert_offsets, const uint16_t* x_sorted,
+                        int64_t P, int hidden, int inter, uint16_t* y_sorted,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Building blocks of moe_layer_forward, exported for tests and for the
  * expert-parallel path (dispatch/combine around an all-to-all).
  *
@@ -184,6 +203,36 @@ int moe_gather_rows(const uint16_t* rows_in, const int32_t* index, int64_t n,
 int moe_combine(const uint16_t* y_sorted, const int32_t* pair_slot,
                 const int64_t* indices, const float* weights, int64_t T, int k,
                 int width, uint16_t* out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Expert-parallel token exchange (one process per GPU; the caller runs the two
+ * all-to-alls, e.g. NCCL, between these steps).  G ranks, E experts, rank r
+ * owns experts [r*E/G, (r+1)*E/G).  Buffers are capacity-padded so both
+ * all-to-alls use equal splits and nothing needs a host synchronisation:
+ * cap >= tokens per rank * min(k, E/G) rows per (source, destination) pair.
+ * Replaces nothing in the reference (single-GPU); it feeds the same per-expert
+ * semantics (model/moe_layer.py:150-191) from tokens of every rank.
+ *
+ * moe_ep_dispatch (source; after moe_permute):
+ *   send_rows fp16 [G*cap, hidden]: send_rows[r*cap+i] = h[pair_token[off[r*E/G]+i]]
+ *   send_counts int32 [E] (tokens per expert, grouped by owner rank)
+ *   pair_slot_ep int32 [T*k]: row of pair t*k+j in the returned buffer
+ * moe_ep_receive (owner; after the all-to-all of rows and counts):
+ *   x_sorted fp16 [G*cap, hidden] grouped by local expert (then source rank),
+ *   local_offsets int32 [E/G + 1]; feed both to moe_experts_forward with P = G*cap.
+ * moe_ep_return (owner): y_back[s*cap+i] = y_sorted[row of (s, i)]; after the
+ *   all-to-all back, moe_combine(y_back, pair_slot_ep, ...) on the source.
+ * Limits: E % G == 0, E <= 32, hidden % 8 == 0.
+ */
+int moe_ep_dispatch(const uint16_t* h, const int32_t* expert_offsets,
+                    const int32_t* pair_token, const int32_t* pair_slot, int64_t T,
+                    int k, int E, int G, int cap, int hidden, uint16_t* send_rows,
+                    int32_t* send_counts, int32_t* pair_slot_ep, void* stream);
+int moe_ep_receive(const uint16_t* recv_rows, const int32_t* recv_counts, int E,
+                   int G, int cap, int hidden, uint16_t* x_sorted,
+                   int32_t* local_offsets, void* stream);
+int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_counts, int E,
+                  int G, int cap, int hidden, uint16_t* y_back, void* stream);
 
 #ifdef __cplusplus
 }

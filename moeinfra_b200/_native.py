@@ -28,6 +28,7 @@ class NF4Expert(ctypes.Structure):
 SIGNATURES: dict[str, tuple] = {
     "moe_status_string": (ctypes.c_char_p, [c_int]),
     "moe_version": (ctypes.c_char_p, []),
+    "moe_launch_count": (ctypes.c_uint64, []),
     "moe_take_device_error": (c_int, [ctypes.POINTER(c_int)]),
     "moe_nf4_dequant": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "moe_nf4_tile16": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
@@ -42,6 +43,9 @@ SIGNATURES: dict[str, tuple] = {
     "moe_expert_workspace_size": (c_size_t, [c_int64, c_int, c_int]),
     "moe_expert_forward": (c_int, [ctypes.POINTER(NF4Expert), c_void_p, c_int64, c_int, c_int,
                                    c_void_p, c_void_p, c_size_t, c_void_p]),
+    "moe_experts_workspace_size": (c_size_t, [c_int64, c_int, c_int]),
+    "moe_experts_forward": (c_int, [ctypes.POINTER(NF4Expert), c_int, c_void_p, c_void_p, c_int64,
+                                    c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "moe_layer_workspace_size": (c_size_t, [c_int64, c_int, c_int, c_int, c_int]),
     "moe_layer_forward": (c_int, [c_void_p, c_void_p, ctypes.POINTER(NF4Expert), c_int, c_int,
                                   c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
@@ -51,6 +55,11 @@ SIGNATURES: dict[str, tuple] = {
     "moe_gather_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "moe_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
                             c_void_p, c_void_p]),
+    "moe_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
+                                c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "moe_ep_receive": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                               c_void_p]),
+    "moe_ep_return": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -80,6 +89,11 @@ def lib() -> ctypes.CDLL:
 
 def status_string(status: int) -> str:
     return lib().moe_status_string(int(status)).decode()
+
+
+def launch_count() -> int:
+    """Kernels launched (or captured) by the library so far in this process."""
+    return int(lib().moe_launch_count())
 
 
 def take_device_error() -> int:

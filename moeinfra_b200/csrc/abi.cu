@@ -1,5 +1,18 @@
-// Status strings and build identification for the C ABI.
+// Status strings, build identification and the launch counter of the C ABI.
+#include <atomic>
+
 #include "common.cuh"
+
+namespace moe {
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+}
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace moe
+
+extern "C" uint64_t moe_launch_count(void) {
+  return moe::g_launches.load(std::memory_order_relaxed);
+}
 
 extern "C" const char* moe_status_string(int status) {
   switch (status) {

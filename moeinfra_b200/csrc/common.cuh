@@ -8,13 +8,18 @@
 
 #include "../../include/moe_b200.h"
 
+// Every kernel launch of the library is followed by this check; it also counts
+// the launch (moe_launch_count), host side, so a CUDA-graph capture of a step
+// reports how many kernels one replay runs.
 #define MOE_CHECK_LAUNCH()                                   \
   do {                                                       \
     cudaError_t _e = cudaGetLastError();                     \
     if (_e != cudaSuccess) return MOE_ERR_CUDA;              \
+    ::moe::note_launch();                                    \
   } while (0)
 
 namespace moe {
+void note_launch();
 
 constexpr int kWarp = 32;
 

@@ -1,0 +1,188 @@
+// Expert-parallel token exchange: the pack / receive / return steps around the
+// two NCCL all-to-alls of an expert-parallel MoE layer.
+//
+// G ranks, E experts, El = E / G local experts: rank r owns experts
+// [r*El, (r+1)*El).  Every buffer exchanged is capacity-padded, so the
+// all-to-alls use equal splits and no step needs a host synchronisation:
+//   cap = max tokens per rank * min(k, El) rows per (source, destination) pair.
+//
+// Source rank, after the router and moe_permute (pairs sorted by expert):
+//   send_rows[r*cap + i]  = h[pair_token[offsets[r*El] + i]],  i < n_r
+//   send_counts[r*El + j] = tokens of expert r*El + j
+//   pair_slot_ep[q]       = r*cap + pair_slot[q] - offsets[r*El]   (r = owner)
+// Destination rank, after the all-to-all (recv[s*cap + i] came from rank s):
+//   x_sorted rows ordered by (local expert j, source s, i); local_offsets[j]
+//   the first row of expert j -- the grouped layout the expert kernels read.
+// Return: y_back[s*cap + i] = y_sorted[row of (s, i)], sent back by a second
+// all-to-all, after which y_back on the source is addressed by pair_slot_ep
+// and moe_combine applies the reference's ordered fp16 combine
+// (model/moe_layer.py:187-191) unchanged.
+#include "common.cuh"
+
+namespace moe {
+namespace {
+
+constexpr int kEpMaxExperts = 32;
+constexpr int kEpThreads = 256;
+
+int grid_rows(int64_t work) {
+  int64_t b = ceil_div(work, kEpThreads);
+  int64_t cap = (int64_t)sm_count() * 8;
+  return static_cast<int>(b < 1 ? 1 : (b < cap ? b : cap));
+}
+
+__global__ void __launch_bounds__(kEpThreads) k_ep_dispatch(
+    const uint4* __restrict__ h, const int32_t* __restrict__ offsets,
+    const int32_t* __restrict__ pair_token, const int32_t* __restrict__ pair_slot, int64_t P,
+    int E, int El, int G, int cap, int vpr, uint4* __restrict__ send,
+    int32_t* __restrict__ send_counts, int32_t* __restrict__ pair_slot_ep) {
+  __shared__ int s_off[kEpMaxExperts + 1];
+  if (threadIdx.x <= E) s_off[threadIdx.x] = offsets[threadIdx.x];
+  __syncthreads();
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (tid < E) send_counts[tid] = s_off[tid + 1] - s_off[tid];
+  for (int64_t q = tid; q < P; q += stride) {
+    const int p = pair_slot[q];
+    int e = 0;
+    while (e + 1 < E && s_off[e + 1] <= p) ++e;
+    const int r = e / El;
+    pair_slot_ep[q] = r * cap + (p - s_off[r * El]);
+  }
+  const int64_t total = (int64_t)G * cap * vpr;
+  for (int64_t v = tid; v < total; v += stride) {
+    const int64_t row = v / vpr;
+    const int c = static_cast<int>(v - row * vpr);
+    const int r = static_cast<int>(row / cap), i = static_cast<int>(row - (int64_t)r * cap);
+    const int p = s_off[r * El] + i;
+    if (p < s_off[(r + 1) * El]) send[row * vpr + c] = h[(int64_t)pair_token[p] * vpr + c];
+  }
+}
+
+// Per-(source, local expert) bases of the receive layout, in shared memory.
+struct RecvPlan {
+  int n[kEpMaxExperts];         // rows from source s (clamped to cap)
+  int src_base[kEpMaxExperts];  // [s*El + j]: first row of expert j within source s's chunk
+  int dst_base[kEpMaxExperts];  // [s*El + j]: first x_sorted row of (j, s)
+  int cnt[kEpMaxExperts];
+  int local_off[kEpMaxExperts + 1];
+};
+
+__device__ void build_plan(const int32_t* __restrict__ counts, int El, int G, int cap,
+                           RecvPlan& pl) {
+  if (threadIdx.x == 0) {
+    // Counts come from peers; clamp so that no source exceeds its cap rows and
+    // every derived row index stays inside the G*cap-row buffers.
+    for (int s = 0; s < G; ++s) {
+      int acc = 0;
+      for (int j = 0; j < El; ++j) {
+        int c = counts[s * El + j];
+        c = c < 0 ? 0 : (c > cap - acc ? cap - acc : c);
+        pl.cnt[s * El + j] = c;
+        pl.src_base[s * El + j] = acc;
+        acc += c;
+      }
+      pl.n[s] = acc;
+    }
+    int acc = 0;
+    for (int j = 0; j < El; ++j) {
+      pl.local_off[j] = acc;
+      for (int s = 0; s < G; ++s) {
+        pl.dst_base[s * El + j] = acc;
+        acc += pl.cnt[s * El + j];
+      }
+    }
+    pl.local_off[El] = acc;
+  }
+  __syncthreads();
+}
+
+// x_sorted row of received row (s, i), or -1 for a padding row.
+__device__ __forceinline__ int64_t recv_dst(const RecvPlan& pl, int El, int s, int i) {
+  if (i >= pl.n[s]) return -1;
+  int j = 0;
+  while (j + 1 < El && pl.src_base[s * El + j + 1] <= i) ++j;
+  return pl.dst_base[s * El + j] + (i - pl.src_base[s * El + j]);
+}
+
+template <bool kReceive>
+__global__ void __launch_bounds__(kEpThreads) k_ep_move(
+    const uint4* __restrict__ in, const int32_t* __restrict__ counts, int El, int G, int cap,
+    int vpr, uint4* __restrict__ out, int32_t* __restrict__ local_offsets) {
+  __shared__ RecvPlan pl;
+  build_plan(counts, El, G, cap, pl);
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (kReceive && tid <= El) local_offsets[tid] = pl.local_off[tid];
+  const int64_t total = (int64_t)G * cap * vpr;
+  const int64_t rows_out = (int64_t)G * cap;
+  for (int64_t v = tid; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = v / vpr;  // (s, i) in the exchanged layout
+    const int c = static_cast<int>(v - row * vpr);
+    const int s = static_cast<int>(row / cap), i = static_cast<int>(row - (int64_t)s * cap);
+    const int64_t dst = recv_dst(pl, El, s, i);
+    if (dst < 0 || dst >= rows_out) continue;
+    if (kReceive)
+      out[dst * vpr + c] = in[row * vpr + c];
+    else
+      out[row * vpr + c] = in[dst * vpr + c];
+  }
+}
+
+bool ep_args_ok(int E, int G, int cap, int hidden) {
+  return G >= 1 && E >= G && E <= kEpMaxExperts && E % G == 0 && cap >= 1 && hidden > 0 &&
+         hidden % 8 == 0;
+}
+
+}  // namespace
+}  // namespace moe
+
+extern "C" int moe_ep_dispatch(const uint16_t* h, const int32_t* expert_offsets,
+                               const int32_t* pair_token, const int32_t* pair_slot, int64_t T,
+                               int k, int E, int G, int cap, int hidden, uint16_t* send_rows,
+                               int32_t* send_counts, int32_t* pair_slot_ep, void* stream) {
+  using namespace moe;
+  if (T < 0 || k < 1 || !ep_args_ok(E, G, cap, hidden)) return MOE_ERR_INVALID_ARG;
+  const int El = E / G;
+  if (T * (k < El ? k : El) > cap) return MOE_ERR_INVALID_ARG;
+  if (!expert_offsets || !send_counts || !send_rows) return MOE_ERR_INVALID_ARG;
+  if (T > 0 && (!h || !pair_token || !pair_slot || !pair_slot_ep)) return MOE_ERR_INVALID_ARG;
+  if ((T > 0 && !aligned16(h)) || !aligned16(send_rows)) return MOE_ERR_ALIGNMENT;
+  const int vpr = hidden / 8;
+  k_ep_dispatch<<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                  static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(h), expert_offsets, pair_token, pair_slot, T * k, E, El, G,
+      cap, vpr, reinterpret_cast<uint4*>(send_rows), send_counts, pair_slot_ep);
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_receive(const uint16_t* recv_rows, const int32_t* recv_counts, int E, int G,
+                              int cap, int hidden, uint16_t* x_sorted, int32_t* local_offsets,
+                              void* stream) {
+  using namespace moe;
+  if (!ep_args_ok(E, G, cap, hidden)) return MOE_ERR_INVALID_ARG;
+  if (!recv_rows || !recv_counts || !x_sorted || !local_offsets) return MOE_ERR_INVALID_ARG;
+  if (!aligned16(recv_rows) || !aligned16(x_sorted)) return MOE_ERR_ALIGNMENT;
+  const int vpr = hidden / 8;
+  k_ep_move<true><<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                    static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(recv_rows), recv_counts, E / G, G, cap, vpr,
+      reinterpret_cast<uint4*>(x_sorted), local_offsets);
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_counts, int E, int G,
+                             int cap, int hidden, uint16_t* y_back, void* stream) {
+  using namespace moe;
+  if (!ep_args_ok(E, G, cap, hidden)) return MOE_ERR_INVALID_ARG;
+  if (!y_sorted || !recv_counts || !y_back) return MOE_ERR_INVALID_ARG;
+  if (!aligned16(y_sorted) || !aligned16(y_back)) return MOE_ERR_ALIGNMENT;
+  const int vpr = hidden / 8;
+  k_ep_move<false><<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                     static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(y_sorted), recv_counts, E / G, G, cap, vpr,
+      reinterpret_cast<uint4*>(y_back), nullptr);
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}

@@ -193,3 +193,52 @@ extern "C" int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t
   }
   return launch_grouped_gemm_experts(expert, 1, b.offsets, x, n, hidden, inter, b.h, y, s);
 }
+
+// ---------------------------------------------------------------------------
+// Expert stage alone: experts applied to already-permuted rows (the tokens of
+// expert e are rows [offsets[e], offsets[e+1]) of x_sorted), y_sorted fp16.
+namespace moe {
+namespace {
+struct StageBufs {
+  uint16_t* h;
+  float* y_part;
+};
+size_t carve_stage(unsigned char* ws, int64_t P, int hidden, int inter, StageBufs* b) {
+  Carver c{ws};
+  b->h = c.take<uint16_t>((size_t)P * inter);
+  b->y_part = use_decode_path(P) ? c.take<float>((size_t)P * decode_splits(inter) * hidden) : nullptr;
+  return c.used;
+}
+}  // namespace
+}  // namespace moe
+
+extern "C" size_t moe_experts_workspace_size(int64_t P, int hidden, int inter) {
+  moe::StageBufs b;
+  if (P < 0) return 0;
+  return moe::carve_stage(nullptr, P, hidden, inter, &b);
+}
+
+extern "C" int moe_experts_forward(const moe_nf4_expert_t* experts, int E,
+                                   const int32_t* expert_offsets, const uint16_t* x_sorted,
+                                   int64_t P, int hidden, int inter, uint16_t* y_sorted,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace moe;
+  if (P < 0 || E < 1 || E > MOE_MAX_EXPERTS) return MOE_ERR_INVALID_ARG;
+  if (!shapes_ok(hidden, inter)) return MOE_ERR_UNSUPPORTED;
+  if (P == 0) return MOE_OK;
+  if (!experts || !expert_offsets || !x_sorted || !y_sorted) return MOE_ERR_INVALID_ARG;
+  if (!experts_aligned(experts, E) || !aligned16(x_sorted) || !aligned16(y_sorted))
+    return MOE_ERR_ALIGNMENT;
+  StageBufs b;
+  const size_t need = carve_stage(static_cast<unsigned char*>(workspace), P, hidden, inter, &b);
+  if (!workspace || workspace_bytes < need) return MOE_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (use_decode_path(P)) {
+    int st = launch_decode_experts(experts, E, expert_offsets, nullptr, x_sorted, hidden, inter,
+                                   b.h, b.y_part, static_cast<int>(P), s);
+    if (st != MOE_OK) return st;
+    return launch_reduce_partials(b.y_part, P, decode_splits(inter), hidden, y_sorted, s);
+  }
+  return launch_grouped_gemm_experts(experts, E, expert_offsets, x_sorted, P, hidden, inter, b.h,
+                                     y_sorted, s);
+}

@@ -1,0 +1,96 @@
+"""Expert parallelism: one process per GPU, experts of a layer sharded over ranks.
+
+Rank ``r`` of ``G`` owns experts ``[r*E/G, (r+1)*E/G)`` of every layer.  Each
+rank routes its own tokens; a layer step is
+
+    router -> permute -> ep_dispatch -> all_to_all(counts), all_to_all(rows)
+           -> ep_receive -> experts (local, grouped) -> ep_return
+           -> all_to_all(rows back) -> combine (ascending expert id)
+
+The exchanged buffers are capacity-padded (``cap = tokens * min(k, E/G)`` rows
+per rank pair), so every all-to-all has equal splits and no step reads a count
+back to the host: the step is a fixed sequence of kernels and NCCL calls.  Per
+token the result equals the single-GPU layer (``model/moe_layer.py:117-211``
+of the reference): each expert sees the same rows and the combine runs in the
+same order with the same roundings.
+"""
+from __future__ import annotations
+
+from typing import Sequence
+
+import torch
+import torch.distributed as dist
+
+from moeinfra_b200 import kernels
+
+
+def owner(expert: int, num_experts: int, world: int) -> int:
+    """Rank that holds ``expert`` (contiguous blocks of E/G experts)."""
+    return expert // (num_experts // world)
+
+
+def local_experts(rank: int, num_experts: int, world: int) -> list[int]:
+    per = num_experts // world
+    return list(range(rank * per, (rank + 1) * per))
+
+
+def capacity(max_tokens: int, top_k: int, num_experts: int, world: int) -> int:
+    """Rows one rank can send another: each token reaches at most min(k, E/G) of its experts."""
+    return max(1, max_tokens * min(top_k, num_experts // world))
+
+
+def check_layout(num_experts: int, world: int) -> None:
+    if world < 1 or num_experts % world:
+        raise ValueError(f"{num_experts} experts cannot be sharded evenly over {world} ranks")
+
+
+class ExpertParallelMoE:
+    """One MoE layer whose experts are sharded over the ranks of ``group``.
+
+    ``router`` is an ``ExpertRouter`` (gate replicated on every rank);
+    ``experts`` are this rank's resident NF4 experts in ascending expert id.
+    ``max_tokens`` bounds the tokens any rank passes per call (it sizes the
+    padded exchange and must be the same on every rank).
+    """
+
+    def __init__(self, router, experts: Sequence, rank: int, world_size: int, max_tokens: int,
+                 group=None) -> None:
+        self.router = router
+        self.num_experts = router.num_experts
+        self.top_k = router.num_experts_per_tok
+        check_layout(self.num_experts, world_size)
+        if len(experts) != self.num_experts // world_size:
+            raise ValueError(f"rank {rank} needs {self.num_experts // world_size} experts, "
+                             f"got {len(experts)}")
+        self.rank, self.world, self.group = rank, world_size, group
+        self.max_tokens = max_tokens
+        self.cap = capacity(max_tokens, self.top_k, self.num_experts, world_size)
+        self.experts = list(experts)
+        self.hidden = experts[0].hidden_size
+        self.inter = experts[0].intermediate_size
+        self._table = kernels.expert_array([ex.nf4_descriptor for ex in self.experts])
+
+    def __call__(self, h: torch.Tensor) -> torch.Tensor:
+        return self.forward(h)
+
+    @torch.no_grad()
+    def forward(self, h: torch.Tensor) -> torch.Tensor:
+        if h.ndim != 2 or h.shape[1] != self.hidden:
+            raise ValueError(f"expected [tokens, {self.hidden}] fp16, got {tuple(h.shape)}")
+        if h.shape[0] > self.max_tokens:
+            raise ValueError(f"{h.shape[0]} tokens exceed max_tokens={self.max_tokens}")
+        h = h.contiguous()
+        E, G, cap, k = self.num_experts, self.world, self.cap, self.top_k
+        _, w, idx = kernels.router_topk(h, self.router.gate_f16(), k, with_logits=False)
+        offsets, pair_token, _, pair_slot = kernels.permute(idx, w, E)
+        send, counts, slot_ep = kernels.ep_dispatch(h, offsets, pair_token, pair_slot, k, E, G, cap)
+        recv_counts = torch.empty_like(counts)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        dist.all_to_all_single(recv, send, group=self.group)
+        x_sorted, local_off = kernels.ep_receive(recv, recv_counts, E, G, cap)
+        y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden, self.inter)
+        y_back = kernels.ep_return(y_sorted, recv_counts, E, G, cap)
+        y_home = torch.empty_like(y_back)
+        dist.all_to_all_single(y_home, y_back, group=self.group)
+        return kernels.combine(y_home, slot_ep, idx, w)

@@ -197,6 +197,24 @@ def layer_forward(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hidden: in
     return out, idx, w
 
 
+def experts_forward(experts, expert_offsets: torch.Tensor, x_sorted: torch.Tensor, hidden: int,
+                    inter: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Expert stage on rows grouped by expert (``expert_offsets`` int32 [E+1] on device)."""
+    dev = _need_cuda("experts_forward", expert_offsets=expert_offsets, x_sorted=x_sorted)
+    _need_dtype("experts_forward", x_sorted, torch.float16, "x_sorted")
+    _need_dtype("experts_forward", expert_offsets, torch.int32, "expert_offsets")
+    P = x_sorted.shape[0]
+    if out is None:
+        out = torch.empty(P, hidden, dtype=torch.float16, device=dev)
+    lib = _native.lib()
+    ws_bytes = lib.moe_experts_workspace_size(P, hidden, inter)
+    ws = _workspace(ws_bytes, dev)
+    check(lib.moe_experts_forward(experts, len(experts), _p(expert_offsets), _p(x_sorted), P,
+                                  hidden, inter, _p(out), _p(ws), ws_bytes, _stream(dev)),
+          "moe_experts_forward")
+    return out
+
+
 def permute(indices: torch.Tensor, weights: torch.Tensor, num_experts: int):
     dev = _need_cuda("permute", indices=indices, weights=weights)
     _need_dtype("permute", indices, torch.int64, "indices")
@@ -234,3 +252,45 @@ def combine(y_sorted: torch.Tensor, pair_slot: torch.Tensor, indices: torch.Tens
     check(_native.lib().moe_combine(_p(y_sorted), _p(pair_slot), _p(indices), _p(weights), T, k,
                                     width, _p(out), _stream(dev)), "moe_combine")
     return out
+
+
+# ---------------------------------------------------------------------------
+# Expert-parallel exchange (pack / receive / return around two all-to-alls)
+# ---------------------------------------------------------------------------
+
+def ep_dispatch(h: torch.Tensor, offsets: torch.Tensor, pair_token: torch.Tensor,
+                pair_slot: torch.Tensor, k: int, num_experts: int, world: int, cap: int):
+    """``(send_rows fp16 [world*cap, H], send_counts int32 [E], pair_slot_ep int32 [T*k])``."""
+    dev = _need_cuda("ep_dispatch", h=h, offsets=offsets)
+    _need_dtype("ep_dispatch", h, torch.float16, "hidden_states")
+    T, H = h.shape
+    send = torch.empty(world * cap, H, dtype=torch.float16, device=dev)
+    counts = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    slot_ep = torch.empty(T * k, dtype=torch.int32, device=dev)
+    check(_native.lib().moe_ep_dispatch(_p(h), _p(offsets), _p(pair_token), _p(pair_slot), T, k,
+                                        num_experts, world, cap, H, _p(send), _p(counts),
+                                        _p(slot_ep), _stream(dev)), "moe_ep_dispatch")
+    return send, counts, slot_ep
+
+
+def ep_receive(recv_rows: torch.Tensor, recv_counts: torch.Tensor, num_experts: int, world: int,
+               cap: int):
+    """``(x_sorted fp16 [world*cap, H], local_offsets int32 [E/world + 1])``."""
+    dev = _need_cuda("ep_receive", recv_rows=recv_rows, recv_counts=recv_counts)
+    H = recv_rows.shape[1]
+    x = torch.empty(world * cap, H, dtype=torch.float16, device=dev)
+    off = torch.empty(num_experts // world + 1, dtype=torch.int32, device=dev)
+    check(_native.lib().moe_ep_receive(_p(recv_rows), _p(recv_counts), num_experts, world, cap, H,
+                                       _p(x), _p(off), _stream(dev)), "moe_ep_receive")
+    return x, off
+
+
+def ep_return(y_sorted: torch.Tensor, recv_counts: torch.Tensor, num_experts: int, world: int,
+              cap: int) -> torch.Tensor:
+    """``y_back fp16 [world*cap, H]`` in the exchanged (source rank, row) layout."""
+    dev = _need_cuda("ep_return", y_sorted=y_sorted, recv_counts=recv_counts)
+    H = y_sorted.shape[1]
+    y_back = torch.empty(world * cap, H, dtype=torch.float16, device=dev)
+    check(_native.lib().moe_ep_return(_p(y_sorted), _p(recv_counts), num_experts, world, cap, H,
+                                      _p(y_back), _stream(dev)), "moe_ep_return")
+    return y_back

@@ -127,6 +127,27 @@ def _dynamic_map_signed() -> torch.Tensor:
     return torch.tensor(sorted(data), dtype=torch.float32)
 
 
+def quantize_nf4_packed(weight: torch.Tensor, blocksize: int = NF4_BLOCKSIZE):
+    """Blockwise NF4 quantization on the weight's own device.
+
+    Returns ``(packed uint8 [numel/2], absmax fp32 [numel/blocksize], code fp32 [16])``
+    in the store layout: nearest code (a value exactly on a midpoint takes the
+    lower code), element 2j in the high nibble of byte j.
+    """
+    flat = weight.detach().to(torch.float32).reshape(-1)
+    if flat.numel() % blocksize:
+        raise ValueError(f"weight numel {flat.numel()} is not a multiple of {blocksize}")
+    code = nf4_code_tensor(flat.device)
+    blocks = flat.view(-1, blocksize)
+    absmax = blocks.abs().amax(dim=1)
+    safe = torch.where(absmax == 0, torch.ones_like(absmax), absmax)
+    normed = (blocks / safe[:, None]).reshape(-1)
+    mids = (code[:-1] + code[1:]) / 2.0
+    idx = torch.bucketize(normed, mids, right=False, out_int32=True).to(torch.uint8)
+    packed = ((idx[0::2] << 4) | idx[1::2]).contiguous()
+    return packed, absmax, code
+
+
 def quantize_nf4(weight: torch.Tensor, compress_statistics: bool = False,
                  blocksize: int = NF4_BLOCKSIZE) -> dict:
     """Quantize a 2-D weight [out, in] to a serialized NF4 projection state.
@@ -139,17 +160,7 @@ def quantize_nf4(weight: torch.Tensor, compress_statistics: bool = False,
     if weight.ndim != 2:
         raise ValueError(f"Expected a 2D weight tensor, got shape {tuple(weight.shape)}")
     out_f, in_f = weight.shape
-    flat = weight.detach().to(torch.float32).reshape(-1)
-    if flat.numel() % blocksize:
-        raise ValueError(f"weight numel {flat.numel()} is not a multiple of {blocksize}")
-    code = nf4_code_tensor(flat.device)
-    blocks = flat.view(-1, blocksize)
-    absmax = blocks.abs().amax(dim=1)
-    safe = torch.where(absmax == 0, torch.ones_like(absmax), absmax)
-    normed = (blocks / safe[:, None]).reshape(-1)
-    mids = (code[:-1] + code[1:]) / 2.0
-    idx = torch.bucketize(normed, mids, right=False).to(torch.uint8)
-    packed = ((idx[0::2] << 4) | idx[1::2]).contiguous()
+    packed, absmax, code = quantize_nf4_packed(weight, blocksize)
     meta = {"quant_type": "nf4", "blocksize": blocksize, "dtype": "bfloat16",
             "shape": [out_f, in_f]}
     st = {"weight": packed.cpu(), "weight.quant_map": code.cpu()}

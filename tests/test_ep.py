@@ -1,0 +1,226 @@
+"""Expert-parallel layer: exchange protocol (gloo, CPU ranks), CUDA exchange kernels
+(G ranks emulated on one GPU) and the NCCL layer on 2+ GPUs.
+
+Expected values come from the oracle with full knowledge of every rank's
+tokens: expert e runs (oracle) on the rows all ranks route to it, ordered by
+source rank then token, and each rank combines its tokens in ascending expert
+id -- what the reference's single-GPU layer does for each rank's batch, with
+the expert's row batch now merged across ranks.
+"""
+from __future__ import annotations
+
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from moeinfra_b200 import ep
+from oracle import ep as oep
+from oracle import moe as omoe
+from oracle import nf4 as onf4
+from oracle import router as orouter
+from tests.helpers import assert_close_fp16, make_experts
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tokens(rank: int, T: int, H: int) -> np.ndarray:
+    return np.random.default_rng(100 + rank).standard_normal((T, H), dtype=np.float32).astype(np.float16)
+
+
+def _gate(E: int, H: int) -> np.ndarray:
+    return (np.random.default_rng(7).standard_normal((E, H), dtype=np.float32) * 0.05).astype(np.float16)
+
+
+def expected_outputs(hs: list, wg: np.ndarray, experts: list, H: int, I: int, k: int) -> list:
+    """Per-rank layer outputs when expert e runs once on the rows of every rank."""
+    E = wg.shape[0]
+    routes = [orouter.route_with_logits(h, wg, k) for h in hs]
+    per_expert = {}
+    for e in range(E):
+        rows, owners = [], []
+        for s, (h, (_, _, idx)) in enumerate(zip(hs, routes)):
+            mask = (idx == e).any(-1)
+            rows.append(h[mask])
+            owners += [s] * int(mask.sum())
+        x = np.concatenate(rows, 0)
+        if len(x):
+            per_expert[e] = (onf4.expert_forward(x, experts[e], H, I), np.array(owners))
+    outs = []
+    for s, (h, (_, w, idx)) in enumerate(zip(hs, routes)):
+        ys = {e: y[own == s] for e, (y, own) in per_expert.items() if (own == s).any()}
+        outs.append(omoe.combine_expert_outputs(h.shape[0], H, idx, w, ys))
+    return outs, routes
+
+
+# ---------------------------------------------------------------------------
+# host logic
+# ---------------------------------------------------------------------------
+
+def test_sharding_helpers():
+    assert [ep.owner(e, 8, 2) for e in range(8)] == [0, 0, 0, 0, 1, 1, 1, 1]
+    assert ep.local_experts(3, 8, 4) == [6, 7]
+    assert ep.capacity(1, 2, 8, 8) == 1 and ep.capacity(1, 2, 8, 2) == 2
+    assert ep.capacity(64, 2, 8, 4) == 128
+    with pytest.raises(ValueError):
+        ep.check_layout(8, 3)
+
+
+def _a2a(out: torch.Tensor, inp: torch.Tensor):
+    """all_to_all_single on fp16 rows through an int32 view (gloo has no fp16 all-to-all)."""
+    if inp.dtype == torch.float16:
+        dist.all_to_all_single(out.view(torch.int32), inp.view(torch.int32))
+    else:
+        dist.all_to_all_single(out, inp)
+
+
+def _gloo_worker(rank: int, world: int, port: int, cases: list):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        for (E, T, H, I, k) in cases:
+            experts = make_experts(3, E, H, I)
+            wg = _gate(E, H)
+            hs = [_tokens(s, T, H) for s in range(world)]
+            want, routes = expected_outputs(hs, wg, experts, H, I, k)
+            _, w, idx = routes[rank]
+            cap = ep.capacity(T, k, E, world)
+            send, counts, slot_ep = oep.dispatch(torch.from_numpy(hs[rank]), torch.from_numpy(idx),
+                                                 E, world, cap)
+            recv_counts = torch.empty_like(counts)
+            _a2a(recv_counts, counts)
+            recv = torch.empty_like(send)
+            _a2a(recv, send)
+            x, local_off = oep.receive(recv, recv_counts, E, world, cap)
+            y_sorted = torch.zeros_like(x)
+            for j, e in enumerate(ep.local_experts(rank, E, world)):
+                lo, hi = int(local_off[j]), int(local_off[j + 1])
+                if hi > lo:
+                    y_sorted[lo:hi] = torch.from_numpy(
+                        onf4.expert_forward(x[lo:hi].numpy(), experts[e], H, I))
+            y_back = oep.give_back(y_sorted, recv_counts, E, world, cap)
+            y_home = torch.empty_like(y_back)
+            _a2a(y_home, y_back)
+            out = oep.combine(y_home, slot_ep, torch.from_numpy(idx), torch.from_numpy(w))
+            assert np.array_equal(out.numpy().view(np.uint16), want[rank].view(np.uint16)), \
+                f"rank {rank} case {(E, T, H, I, k)}"
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_protocol_gloo(world):
+    cases = [(8, 3, 64, 128, 2), (8, 1, 64, 128, 2), (4 * world // 2, 5, 64, 128, 2)]
+    mp.start_processes(_gloo_worker, args=(world, _free_port(), cases), nprocs=world,
+                       start_method="spawn")
+
+
+# ---------------------------------------------------------------------------
+# CUDA exchange kernels, G ranks emulated in one process on one GPU
+# ---------------------------------------------------------------------------
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("G,T", [(2, 1), (4, 1), (8, 1), (2, 2)])
+def test_ep_kernels_emulated(G, T):
+    from moeinfra_b200 import kernels
+    from tests.helpers import gpu_expert
+
+    E, H, I, k = 8, 256, 512, 2
+    experts_np = make_experts(5, E, H, I)
+    experts = [gpu_expert(ex, H, I) for ex in experts_np]
+    wg_np = _gate(E, H)
+    wg = torch.from_numpy(wg_np).cuda()
+    hs = [_tokens(s, T, H) for s in range(G)]
+    want, _ = expected_outputs(hs, wg_np, experts_np, H, I, k)
+    cap = ep.capacity(T, k, E, G)
+    El = E // G
+    src = []
+    for s in range(G):
+        h = torch.from_numpy(hs[s]).cuda()
+        _, w, idx = kernels.router_topk(h, wg, k, with_logits=False)
+        off, ptok, _, pslot = kernels.permute(idx, w, E)
+        send, counts, slot_ep = kernels.ep_dispatch(h, off, ptok, pslot, k, E, G, cap)
+        o_send, o_counts, o_slot = oep.dispatch(torch.from_numpy(hs[s]), idx.cpu(), E, G, cap)
+        assert torch.equal(counts.cpu(), o_counts)
+        assert torch.equal(slot_ep.cpu(), o_slot)
+        for r in range(G):
+            n = int(o_counts[r * El:(r + 1) * El].sum())
+            assert torch.equal(send[r * cap:r * cap + n].cpu().view(torch.int16),
+                               o_send[r * cap:r * cap + n].view(torch.int16))
+        src.append((h, w, idx, send, counts, slot_ep))
+    backs = []
+    for r in range(G):
+        recv = torch.cat([src[s][3][r * cap:(r + 1) * cap] for s in range(G)])
+        recv_counts = torch.cat([src[s][4][r * El:(r + 1) * El] for s in range(G)])
+        x, local_off = kernels.ep_receive(recv, recv_counts, E, G, cap)
+        o_x, o_off = oep.receive(recv.cpu(), recv_counts.cpu(), E, G, cap)
+        assert torch.equal(local_off.cpu(), o_off)
+        n = int(o_off[-1])
+        assert torch.equal(x[:n].cpu().view(torch.int16), o_x[:n].view(torch.int16))
+        table = kernels.expert_array([experts[e].nf4_descriptor for e in ep.local_experts(r, E, G)])
+        y = kernels.experts_forward(table, local_off, x, H, I)
+        y_back = kernels.ep_return(y, recv_counts, E, G, cap)
+        o_back = oep.give_back(y.cpu(), recv_counts.cpu(), E, G, cap)
+        _, dst = oep.receive_plan(recv_counts.cpu(), E, G)
+        for s in range(G):
+            m = len(dst[s])
+            assert torch.equal(y_back[s * cap:s * cap + m].cpu().view(torch.int16),
+                               o_back[s * cap:s * cap + m].view(torch.int16))
+        backs.append(y_back)
+    for s in range(G):
+        h, w, idx, _, _, slot_ep = src[s]
+        y_home = torch.cat([backs[r][s * cap:(s + 1) * cap] for r in range(G)])
+        out = kernels.combine(y_home, slot_ep, idx, w)
+        assert_close_fp16(out.cpu().numpy(), want[s], what=f"EP G={G} rank {s}")
+
+
+# ---------------------------------------------------------------------------
+# NCCL layer on 2+ GPUs
+# ---------------------------------------------------------------------------
+
+def _nccl_worker(rank: int, world: int, port: int):
+    from moeinfra_b200.engine.router import ExpertRouter
+    from tests.helpers import gpu_expert
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        E, H, I, k = 8, 256, 512, 2
+        experts_np = make_experts(5, E, H, I)
+        wg_np = _gate(E, H)
+        for T in (1,):
+            hs = [_tokens(s, T, H) for s in range(world)]
+            want, _ = expected_outputs(hs, wg_np, experts_np, H, I, k)
+            layer = ep.ExpertParallelMoE(
+                ExpertRouter(torch.from_numpy(wg_np).cuda(), num_experts_per_tok=k),
+                [gpu_expert(experts_np[e], H, I) for e in ep.local_experts(rank, E, world)],
+                rank=rank, world_size=world, max_tokens=T)
+            out = layer(torch.from_numpy(hs[rank]).cuda())
+            torch.cuda.synchronize()
+            assert_close_fp16(out.cpu().numpy(), want[rank], what=f"NCCL EP rank {rank} T={T}")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_ep_layer_nccl():
+    world = min(torch.cuda.device_count(), 8)
+    world = 8 if world >= 8 else (4 if world >= 4 else 2)
+    mp.start_processes(_nccl_worker, args=(world, _free_port()), nprocs=world,
+                       start_method="spawn")
