@@ -166,6 +166,32 @@ int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
                       void* stream);
 
 /* ---------------------------------------------------------------------------
+ * moe_layer_forward without a workspace argument.  No counterpart in the
+ * reference (its layer allocates through PyTorch on every call).
+ *
+ * For callers that cannot hand the library device memory per call: C or FFI
+ * hosts that bind only plain pointers and have no device allocator of their
+ * own (a ctypes/cgo stub), and serving loops that must not allocate in the
+ * steady state (cudaMalloc synchronises the device, and an allocator that
+ * grows mid-step stalls the step).  Scratch comes from a file-scope device
+ * array of MOE_NOALLOC_SCRATCH_BYTES (4 MiB) per device: enough for
+ * T*k <= 16 routed pairs at Mixtral shapes (hidden 4096, inter 14336), i.e.
+ * decode batches up to 8 tokens with top-2.  A call whose
+ * moe_layer_workspace_size() exceeds it returns MOE_ERR_WORKSPACE and does
+ * nothing.  The array's address is looked up (cudaGetSymbolAddress) on the
+ * first call on each device and cached; make that first call before any
+ * stream capture on the device.  Calls that overlap on one device (other
+ * streams or host threads without ordering) race on the one array: serialise
+ * them.  Nothing in the array needs to start at zero.  Same results as
+ * moe_layer_forward.
+ */
+#define MOE_NOALLOC_SCRATCH_BYTES ((size_t)4 << 20)
+int moe_layer_forward_noalloc(const uint16_t* h, const uint16_t* wg,
+                              const moe_nf4_expert_t* experts, int E, int k,
+                              int64_t T, int hidden, int inter, uint16_t* out,
+                              int64_t* indices, float* weights, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Expert stage alone: SwiGLU experts on rows already grouped by expert (the
  * rows of expert e are [expert_offsets[e], expert_offsets[e+1]) of x_sorted,
  * device int32 [E+1]); y_sorted fp16 [P, hidden] in the same order.  Used after

@@ -14,6 +14,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmoe_b200.so"
 
 MOE_MAX_EXPERTS = 16
+MOE_NOALLOC_SCRATCH_BYTES = 4 << 20
 
 
 class NF4Matrix(ctypes.Structure):
@@ -43,6 +44,9 @@ SIGNATURES: dict[str, tuple] = {
     "moe_expert_workspace_size": (c_size_t, [c_int64, c_int, c_int]),
     "moe_expert_forward": (c_int, [ctypes.POINTER(NF4Expert), c_void_p, c_int64, c_int, c_int,
                                    c_void_p, c_void_p, c_size_t, c_void_p]),
+    "moe_layer_forward_noalloc": (c_int, [c_void_p, c_void_p, ctypes.POINTER(NF4Expert), c_int,
+                                          c_int, c_int64, c_int, c_int, c_void_p, c_void_p,
+                                          c_void_p, c_void_p]),
     "moe_experts_workspace_size": (c_size_t, [c_int64, c_int, c_int]),
     "moe_experts_forward": (c_int, [ctypes.POINTER(NF4Expert), c_int, c_void_p, c_void_p, c_int64,
                                     c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -197,6 +197,27 @@ def layer_forward(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hidden: in
     return out, idx, w
 
 
+def layer_forward_noalloc(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hidden: int,
+                          inter: int, out: torch.Tensor | None = None):
+    """:func:`layer_forward` with the library's own static device scratch (no workspace).
+
+    At most ``MOE_NOALLOC_SCRATCH_BYTES`` of scratch; calls overlapping on one
+    device must be serialised.
+    """
+    dev = _need_cuda("layer_forward_noalloc", h=h, wg=wg)
+    _need_dtype("layer_forward_noalloc", h, torch.float16, "hidden_states")
+    _need_dtype("layer_forward_noalloc", wg, torch.float16, "gate_weight")
+    T = h.shape[0]
+    if out is None:
+        out = torch.empty(T, hidden, dtype=torch.float16, device=dev)
+    idx = torch.empty(T, k, dtype=torch.int64, device=dev)
+    w = torch.empty(T, k, dtype=torch.float32, device=dev)
+    check(_native.lib().moe_layer_forward_noalloc(_p(h), _p(wg), experts, len(experts), k, T,
+                                                  hidden, inter, _p(out), _p(idx), _p(w),
+                                                  _stream(dev)), "moe_layer_forward_noalloc")
+    return out, idx, w
+
+
 def experts_forward(experts, expert_offsets: torch.Tensor, x_sorted: torch.Tensor, hidden: int,
                     inter: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """Expert stage on rows grouped by expert (``expert_offsets`` int32 [E+1] on device)."""
