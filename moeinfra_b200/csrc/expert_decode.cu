@@ -171,11 +171,11 @@ __device__ __forceinline__ Active load_active(const DecodeArgs& a, int* s_off, i
 }
 
 // x words of this thread for blocks [blk0, blk0+NBW): elements blk*64+16t..+16
-// of the token its B column carries (zeros past the expert's token count).
+// of the token its B column carries (zeros past the expert's token count or
+// past the row's last block).
 template <int NBW>
 __device__ __forceinline__ void load_x(const uint16_t* row, bool valid, int blk0, int blk_end,
-                                       int lane, uint32_t (*xr)[8]) {
-  const int t = lane & 3;
+                                       int t, uint32_t (*xr)[8]) {
 #pragma unroll
   for (int kb = 0; kb < NBW; ++kb) {
     uint4 u0 = make_uint4(0, 0, 0, 0), u1 = u0;
@@ -189,43 +189,44 @@ __device__ __forceinline__ void load_x(const uint16_t* row, bool valid, int blk0
   }
 }
 
-// Items per reduction batch: one barrier per batch; partials of two batches
+// Items per reduction batch (one barrier per batch); partials of two batches
 // live in the dynamic shared memory below the table window.
 template <bool kMulti>
-constexpr int batch_items() { return kMulti ? 2 : 4; }
+constexpr int batch_items() { return kMulti ? 2 : 8; }
 template <bool kMulti>
 constexpr int red_cols() { return kMulti ? kMaxTok : 1; }
 template <bool kMulti>
 constexpr int red_floats() { return 2 * batch_items<kMulti>() * kWarpsK * 16 * red_cols<kMulti>(); }
 
-// Register-resident loads of one item (this warp's K part, rows g and g+8).
+// Register-resident loads of one item: MMA rows g (qa, sa) and g+8 (qb, sb),
+// blocks kb of this warp's K part.
 template <int NBW>
 struct ItemLoads {
   uint2 qa[NBW], qb[NBW];
   float sa[NBW], sb[NBW];
 };
 
-// Loads of MMA rows A (tile row ra) and B (tile row rb_) of matrices ma / mb,
-// blocks [blk0, blk0+NBW) of tile rb, skipping blocks >= blk_end.
-template <int NBW>
-__device__ __forceinline__ void load_item(ItemLoads<NBW>& L, const moe_nf4_matrix_t& ma, int ra,
-                                          const moe_nf4_matrix_t& mb, int rb_, int rb, int nblk,
-                                          int blk0, int blk_end, int t) {
+// qa/qb: byte pointers of the thread's 8-byte segment of block 0 (rows g and
+// g+8); consecutive blocks are 512 bytes apart, their absmax 16 floats apart.
+// Blocks with !valid(kb) read as code 7 (0.0) with absmax 0.
+template <int NBW, bool kFull>
+__device__ __forceinline__ void load_item(ItemLoads<NBW>& L, const uint8_t* qa, const uint8_t* qb,
+                                          const float* sa, const float* sb, int kb_valid) {
 #pragma unroll
   for (int kb = 0; kb < NBW; ++kb) {
-    L.qa[kb] = L.qb[kb] = make_uint2(0x77777777u, 0x77777777u);  // NF4 code 7 == 0.0
-    L.sa[kb] = L.sb[kb] = 0.f;
-    if (blk0 + kb < blk_end) {
-      const int64_t seg = ((int64_t)rb * nblk + blk0 + kb) * 16;
-      L.qa[kb] = ldg_stream64(ma.q + (seg + ra) * 32 + t * 8);
-      L.qb[kb] = ldg_stream64(mb.q + (seg + rb_) * 32 + t * 8);
-      L.sa[kb] = __ldg(ma.absmax + seg + ra);
-      L.sb[kb] = __ldg(mb.absmax + seg + rb_);
+    if (kFull || kb < kb_valid) {
+      L.qa[kb] = ldg_stream64(qa + kb * 512);
+      L.qb[kb] = ldg_stream64(qb + kb * 512);
+      L.sa[kb] = __ldg(sa + kb * 16);
+      L.sb[kb] = __ldg(sb + kb * 16);
+    } else {
+      L.qa[kb] = L.qb[kb] = make_uint2(0x77777777u, 0x77777777u);  // NF4 code 7 == 0.0
+      L.sa[kb] = L.sb[kb] = 0.f;
     }
   }
 }
 
-// acc[0..1] = MMA row A (columns 2t, 2t+1), acc[2..3] = MMA row B.
+// acc[0..1] = MMA row g (columns 2t, 2t+1), acc[2..3] = MMA row g+8.
 template <int NBW, bool kMulti>
 __device__ __forceinline__ void compute_item(const ItemLoads<NBW>& L, const uint32_t (*xr)[8],
                                              uint32_t base, float* acc) {
@@ -270,204 +271,252 @@ __device__ __forceinline__ float reduce_partials(const float* red, int slot, int
   return s;
 }
 
+// Where a reduced item goes (written by thread 0 before the batch barrier).
+struct SlotMeta {
+  int tok0;  // first sorted pair of the item's expert
+  int n;     // tokens of that expert
+  int row;   // first output row of the item
+  int s;     // down: K split
+};
+
+// Item order of a CTA: (active expert ai, index r within the expert), r
+// fastest; advanced without division.
+struct Cursor {
+  int ai, r;
+  __device__ __forceinline__ void next(int per) {
+    if (++r == per) {
+      r = 0;
+      ++ai;
+    }
+  }
+};
+
 // gate_up.  NBW = 64-element blocks per warp (16 warps split H).  Item = 8 rows
-// of W1 and the same 8 rows of W3 (one MMA).
-template <int NBW, bool kMulti>
+// of W1 and the same 8 rows of W3 (one MMA), r = 2*tile + half.
+template <int NBW, bool kMulti, bool kFull>
 __global__ void __launch_bounds__(kThreadsK, 1) k_gate_up_mma(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_off[MOE_MAX_EXPERTS + 1];
   __shared__ int s_active[MOE_MAX_EXPERTS];
   constexpr int B = batch_items<kMulti>();
+  __shared__ SlotMeta s_meta[2 * B];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  Active act;
-  float* red = nullptr;
-  {
-    act = load_active<kMulti>(a, s_off, s_active);
-    if (act.n == 0) return;
-    if (smem_u32(smem) + red_floats<kMulti>() * 4 > kLutWin) return;
-    if (!build_lut(a.ex.e[act.first].w1.code, smem)) return;
-    red = reinterpret_cast<float*>(smem);
-  }
+  const Active act = load_active<kMulti>(a, s_off, s_active);
+  if (act.n == 0) return;
+  if (smem_u32(smem) + red_floats<kMulti>() * 4 > kLutWin) return;
+  if (!build_lut(a.ex.e[act.first].w1.code, smem)) return;
+  float* red = reinterpret_cast<float*>(smem);
+
   const int H = a.H, I = a.I;
   const int nblk = H / 64;
-  const int items_per_expert = I / 8;  // half tiles of 8 rows
-  const int total = act.n * items_per_expert;
+  const int per = I / 8;
   int first, last;
-  cta_range(total, &first, &last);
+  cta_range(act.n * per, &first, &last);
   const int my_items = last - first;
+  if (my_items <= 0) return;
   const uint32_t base = kMulti ? (kLutWin | 128u | ((lane & 15) * 8)) : (kLutWin | (lane * 4));
   const int blk0 = warp * NBW;
-  int staged = -1;
-  uint32_t xr[NBW][8];
-  ItemLoads<NBW> cur, nxt;
+  const int kb_valid = nblk - blk0;  // blocks of this warp inside the row
+  const int64_t tile_q = (int64_t)nblk * 512, tile_s = (int64_t)nblk * 16;
+  const int thr_q = blk0 * 512 + g * 32 + t * 8, thr_s = blk0 * 16 + g;
 
-  auto item_of = [&](int i) { return first + i; };
-  // One thread pulls the whole 16-row tile (W1, W3, both absmax) of an upcoming
-  // item into L2 when that item starts a tile (or starts this CTA's range).
-  auto prefetch = [&](int i) {
-    if (threadIdx.x != 0 || i >= my_items) return;
-    const int item = item_of(i);
-    const int hi = item % items_per_expert;
-    if ((hi & 1) && i != 0) return;
-    const moe_nf4_expert_t& ex = a.ex.e[s_active[item / items_per_expert]];
-    const int64_t tile = hi >> 1;
-    const uint32_t qbytes = 16u * (H / 2), abytes = 16u * (H / 64) * 4u;
-    prefetch_l2(ex.w1.q + tile * qbytes, qbytes);
-    prefetch_l2(ex.w3.q + tile * qbytes, qbytes);
-    prefetch_l2(ex.w1.absmax + tile * (abytes / 4), abytes);
-    prefetch_l2(ex.w3.absmax + tile * (abytes / 4), abytes);
+  uint32_t xr[NBW][8];
+  ItemLoads<NBW> L0, L1;
+  Cursor ld{first / per, first % per};  // next item to load
+  Cursor cp = ld;                       // next item to compute
+  const moe_nf4_expert_t* ld_ex = &a.ex.e[s_active[ld.ai]];
+  int staged = -1;
+
+  auto issue = [&](ItemLoads<NBW>& L) {
+    const int tile = ld.r >> 1, half = ld.r & 1;
+    const int64_t qo = tile * tile_q + half * 256 + thr_q;
+    const int64_t so = tile * tile_s + half * 8 + thr_s;
+    load_item<NBW, kFull>(L, ld_ex->w1.q + qo, ld_ex->w3.q + qo, ld_ex->w1.absmax + so,
+                          ld_ex->w3.absmax + so, kb_valid);
+    const int ai = ld.ai;
+    ld.next(per);
+    if (ld.ai != ai && ld.ai < act.n) ld_ex = &a.ex.e[s_active[ld.ai]];
   };
-  for (int i = 0; i < kPrefetchItems && i < my_items; ++i) prefetch(i);
-  auto issue = [&](ItemLoads<NBW>& L, int i) {
-    const int item = item_of(i);
-    const moe_nf4_expert_t& ex = a.ex.e[s_active[item / items_per_expert]];
-    const int hi = item % items_per_expert;
-    const int rsub = (hi & 1) * 8 + g;
-    load_item<NBW>(L, ex.w1, rsub, ex.w3, rsub, hi >> 1, nblk, blk0, nblk, t);
+  // One thread pulls the whole 16-row tile (W1, W3, both absmax) of an item
+  // kPrefetchItems ahead into L2 when that item starts a tile.
+  Cursor pf = cp;
+  auto prefetch = [&]() {
+    if (pf.ai < act.n && (pf.r & 1) == 0) {
+      const moe_nf4_expert_t& ex = a.ex.e[s_active[pf.ai]];
+      const int64_t tile = pf.r >> 1;
+      const uint32_t qbytes = 16u * (H / 2), abytes = 16u * (H / 64) * 4u;
+      prefetch_l2(ex.w1.q + tile * qbytes, qbytes);
+      prefetch_l2(ex.w3.q + tile * qbytes, qbytes);
+      prefetch_l2(ex.w1.absmax + tile * (abytes / 4), abytes);
+      prefetch_l2(ex.w3.absmax + tile * (abytes / 4), abytes);
+    }
+    pf.next(per);
   };
-  if (my_items > 0) issue(cur, 0);
-  for (int i = 0; i < my_items; ++i) {
-    prefetch(i + kPrefetchItems);
-    if (i + 1 < my_items) issue(nxt, i + 1);
-    const int item = item_of(i);
-    const int e = s_active[item / items_per_expert];
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kPrefetchItems; ++i) prefetch();
+
+  auto body = [&](const ItemLoads<NBW>& L, int i) {
+    if (threadIdx.x == 0) prefetch();
+    const int e = s_active[cp.ai];
     const int tok0 = s_off[e];
     const int n = s_off[e + 1] - tok0;
-    if (e != staged) {
+    if (cp.ai != staged) {
       const int tok = kMulti ? g : 0;
       const bool valid = tok < n;
       const int64_t xrow =
           valid ? (a.pair_token ? a.pair_token[tok0 + tok] : (int64_t)(tok0 + tok)) : 0;
-      load_x<NBW>(a.x + xrow * H, valid, blk0, nblk, lane, xr);
-      staged = e;
+      load_x<NBW>(a.x + xrow * H, valid, blk0, nblk, t, xr);
+      staged = cp.ai;
     }
     float acc[4];
-    compute_item<NBW, kMulti>(cur, xr, base, acc);
-    const int slot = (i / B) % 2 * B + i % B;
+    compute_item<NBW, kMulti>(L, xr, base, acc);
+    const int slot = ((i / B) & 1) * B + i % B;
     stash<kMulti>(red, slot, warp, g, t, acc);
+    if (threadIdx.x == 0) s_meta[slot] = SlotMeta{tok0, n, (cp.r >> 1) * 16 + (cp.r & 1) * 8, 0};
+    cp.next(per);
     if (i % B == B - 1 || i == my_items - 1) {
       __syncthreads();
-      // Finalize the batch: items i0..i of this batch, 8 rows x tokens each.
-      const int i0 = i - i % B;
-      const int nb = i - i0 + 1;
-      for (int job = threadIdx.x; job < nb * 8 * kMaxTok; job += blockDim.x) {
-        const int bi = job / (8 * kMaxTok), rem = job % (8 * kMaxTok);
+      // Finalize the batch: 8 rows x tokens of each of its items.
+      const int i0 = i - i % B, sl0 = ((i0 / B) & 1) * B;
+      const int jobs = (i - i0 + 1) * 8 * red_cols<kMulti>();
+      for (int job = threadIdx.x; job < jobs; job += kThreadsK) {
+        const int bi = job / (8 * red_cols<kMulti>()), rem = job % (8 * red_cols<kMulti>());
         const int rr = rem & 7, tok = rem >> 3;
-        const int it2 = item_of(i0 + bi);
-        const int e2 = s_active[it2 / items_per_expert];
-        const int t0 = s_off[e2], n2 = s_off[e2 + 1] - t0;
-        if (tok >= (kMulti ? n2 : 1)) continue;
-        const int sl = ((i0 + bi) / B) % 2 * B + bi;
-        const float gs = reduce_partials<kMulti>(red, sl, rr, kMulti ? tok : 0);
-        const float us = reduce_partials<kMulti>(red, sl, rr + 8, kMulti ? tok : 0);
-        const int hi = it2 % items_per_expert;
-        const int r = (hi >> 1) * 16 + (hi & 1) * 8 + rr;
-        a.h_sorted[(int64_t)(t0 + tok) * I + r] = swiglu_f16(f2h(gs), f2h(us));
+        const SlotMeta m = s_meta[sl0 + bi];
+        if (tok >= m.n) continue;
+        const float gs = reduce_partials<kMulti>(red, sl0 + bi, rr, tok);
+        const float us = reduce_partials<kMulti>(red, sl0 + bi, rr + 8, tok);
+        a.h_sorted[(int64_t)(m.tok0 + tok) * I + m.row + rr] = swiglu_f16(f2h(gs), f2h(us));
       }
     }
-    cur = nxt;
+  };
+
+  issue(L0);
+  for (int i = 0; i < my_items; i += 2) {
+    if (i + 1 < my_items) issue(L1);
+    body(L0, i);
+    if (i + 1 >= my_items) break;
+    if (i + 2 < my_items) issue(L0);
+    body(L1, i + 1);
   }
 }
 
 // down.  NBW = 64-element blocks per warp of one 2048-element split.  Item =
-// (split s, tile of 16 W2 rows).
-template <int NBW, bool kMulti>
+// (split s, tile rb of 16 W2 rows), rb fastest: r = s * tiles + rb.
+template <int NBW, bool kMulti, bool kFull>
 __global__ void __launch_bounds__(kThreadsK, 1) k_down_mma(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_off[MOE_MAX_EXPERTS + 1];
   __shared__ int s_active[MOE_MAX_EXPERTS];
   constexpr int B = batch_items<kMulti>();
+  constexpr int kSplitBlocks = kDownSlice / 64;
+  __shared__ SlotMeta s_meta[2 * B];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  Active act;
-  float* red = nullptr;
-  {
-    act = load_active<kMulti>(a, s_off, s_active);
-    if (act.n == 0) return;
-    if (smem_u32(smem) + red_floats<kMulti>() * 4 > kLutWin) return;
-    if (!build_lut(a.ex.e[act.first].w2.code, smem)) return;
-    red = reinterpret_cast<float*>(smem);
-  }
+  const Active act = load_active<kMulti>(a, s_off, s_active);
+  if (act.n == 0) return;
+  if (smem_u32(smem) + red_floats<kMulti>() * 4 > kLutWin) return;
+  if (!build_lut(a.ex.e[act.first].w2.code, smem)) return;
+  float* red = reinterpret_cast<float*>(smem);
+
   const int H = a.H, I = a.I;
   const int nblk = I / 64;
   const int tiles = H / 16;
-  const int items_per_expert = a.S * tiles;
-  const int total = act.n * items_per_expert;
+  const int per = a.S * tiles;
   int first, last;
-  cta_range(total, &first, &last);
+  cta_range(act.n * per, &first, &last);
   const int my_items = last - first;
+  if (my_items <= 0) return;
   const uint32_t base = kMulti ? (kLutWin | 128u | ((lane & 15) * 8)) : (kLutWin | (lane * 4));
-  int staged_e = -1, staged_s = -1;
-  uint32_t xr[NBW][8];
-  ItemLoads<NBW> cur, nxt;
+  const int wblk = warp * NBW;  // this warp's first block within a split
+  const int64_t tile_q = (int64_t)nblk * 512, tile_s = (int64_t)nblk * 16;
+  const int thr_q = wblk * 512 + g * 32 + t * 8, thr_s = wblk * 16 + g;
 
-  auto item_of = [&](int i) { return first + i; };
-  // One thread pulls an upcoming item's blocks (contiguous in tile16) into L2.
-  auto prefetch = [&](int i) {
-    if (threadIdx.x != 0 || i >= my_items) return;
-    const int item = item_of(i);
-    const moe_nf4_expert_t& ex = a.ex.e[s_active[item / items_per_expert]];
-    const int rem = item % items_per_expert;
-    const int s = rem / tiles, rb = rem % tiles;
-    const int b0 = s * (kDownSlice / 64), b1 = min(b0 + kDownSlice / 64, nblk);
-    const int64_t seg0 = ((int64_t)rb * nblk + b0) * 16;
-    prefetch_l2(ex.w2.q + seg0 * 32, (uint32_t)(b1 - b0) * 512u);
-    prefetch_l2(ex.w2.absmax + seg0, (uint32_t)(b1 - b0) * 64u);
-  };
-  for (int i = 0; i < kPrefetchItems && i < my_items; ++i) prefetch(i);
-  auto issue = [&](ItemLoads<NBW>& L, int i) {
-    const int item = item_of(i);
-    const moe_nf4_expert_t& ex = a.ex.e[s_active[item / items_per_expert]];
-    const int rem = item % items_per_expert;
-    const int s = rem / tiles, rb = rem % tiles;
-    const int b0 = s * (kDownSlice / 64) + warp * NBW;
-    const int bend = min((s + 1) * (kDownSlice / 64), nblk);
-    load_item<NBW>(L, ex.w2, g, ex.w2, g + 8, rb, nblk, b0, bend, t);
-  };
-  if (my_items > 0) issue(cur, 0);
-  for (int i = 0; i < my_items; ++i) {
-    prefetch(i + kPrefetchItems);
-    if (i + 1 < my_items) issue(nxt, i + 1);
-    const int item = item_of(i);
-    const int e = s_active[item / items_per_expert];
-    const int rem = item % items_per_expert;
-    const int s = rem / tiles;
-    const int tok0 = s_off[e];
-    const int n = s_off[e + 1] - tok0;
-    if (e != staged_e || s != staged_s) {
-      const int blk0 = s * (kDownSlice / 64) + warp * NBW;
-      const int blk_end = min((s + 1) * (kDownSlice / 64), nblk);
-      const int tok = kMulti ? g : 0;
-      const bool valid = tok < n;
-      load_x<NBW>(a.h_sorted + (int64_t)(tok0 + (valid ? tok : 0)) * I, valid, blk0, blk_end,
-                  lane, xr);
-      staged_e = e;
-      staged_s = s;
-    }
-    float acc[4];
-    compute_item<NBW, kMulti>(cur, xr, base, acc);
-    const int slot = (i / B) % 2 * B + i % B;
-    stash<kMulti>(red, slot, warp, g, t, acc);
-    if (i % B == B - 1 || i == my_items - 1) {
-      __syncthreads();
-      const int i0 = i - i % B;
-      const int nb = i - i0 + 1;
-      for (int job = threadIdx.x; job < nb * 16 * kMaxTok; job += blockDim.x) {
-        const int bi = job / (16 * kMaxTok), rem2 = job % (16 * kMaxTok);
-        const int rr = rem2 & 15, tok = rem2 >> 4;
-        const int it2 = item_of(i0 + bi);
-        const int e2 = s_active[it2 / items_per_expert];
-        const int t0 = s_off[e2], n2 = s_off[e2 + 1] - t0;
-        if (tok >= (kMulti ? n2 : 1)) continue;
-        const int sl = ((i0 + bi) / B) % 2 * B + bi;
-        const float ys = reduce_partials<kMulti>(red, sl, rr, kMulti ? tok : 0);
-        const int r2 = it2 % items_per_expert;
-        const int s2 = r2 / tiles, rb2 = r2 % tiles;
-        a.y_part[((int64_t)(t0 + tok) * a.S + s2) * H + rb2 * 16 + rr] = ys;
+  uint32_t xr[NBW][8];
+  ItemLoads<NBW> L0, L1;
+  // (ai, s, rb) of the next item to load / compute.
+  int l_ai = first / per, l_r = first % per;
+  int l_s = l_r / tiles, l_rb = l_r % tiles;
+  int c_ai = l_ai, c_s = l_s, c_rb = l_rb;
+  const moe_nf4_expert_t* ld_ex = &a.ex.e[s_active[l_ai]];
+  int staged_ai = -1, staged_s = -1;
+  auto step = [&](int& ai, int& s, int& rb) {
+    if (++rb == tiles) {
+      rb = 0;
+      if (++s == a.S) {
+        s = 0;
+        ++ai;
       }
     }
-    cur = nxt;
+  };
+
+  auto issue = [&](ItemLoads<NBW>& L) {
+    const int64_t qo = l_rb * tile_q + (int64_t)l_s * kSplitBlocks * 512 + thr_q;
+    const int64_t so = l_rb * tile_s + (int64_t)l_s * kSplitBlocks * 16 + thr_s;
+    const uint8_t* q = ld_ex->w2.q + qo;
+    const float* sc = ld_ex->w2.absmax + so;
+    load_item<NBW, kFull>(L, q, q + 256, sc, sc + 8, nblk - l_s * kSplitBlocks - wblk);
+    const int ai = l_ai;
+    step(l_ai, l_s, l_rb);
+    if (l_ai != ai && l_ai < act.n) ld_ex = &a.ex.e[s_active[l_ai]];
+  };
+  // One thread pulls an upcoming item's blocks (contiguous in tile16) into L2.
+  int p_ai = c_ai, p_s = c_s, p_rb = c_rb;
+  auto prefetch = [&]() {
+    if (p_ai < act.n) {
+      const moe_nf4_expert_t& ex = a.ex.e[s_active[p_ai]];
+      const int b0 = p_s * kSplitBlocks, b1 = min(b0 + kSplitBlocks, nblk);
+      const int64_t seg0 = ((int64_t)p_rb * nblk + b0) * 16;
+      prefetch_l2(ex.w2.q + seg0 * 32, (uint32_t)(b1 - b0) * 512u);
+      prefetch_l2(ex.w2.absmax + seg0, (uint32_t)(b1 - b0) * 64u);
+    }
+    step(p_ai, p_s, p_rb);
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kPrefetchItems; ++i) prefetch();
+
+  auto body = [&](const ItemLoads<NBW>& L, int i) {
+    if (threadIdx.x == 0) prefetch();
+    const int e = s_active[c_ai];
+    const int tok0 = s_off[e];
+    const int n = s_off[e + 1] - tok0;
+    if (c_ai != staged_ai || c_s != staged_s) {
+      const int blk0 = c_s * kSplitBlocks + wblk;
+      const int tok = kMulti ? g : 0;
+      const bool valid = tok < n;
+      load_x<NBW>(a.h_sorted + (int64_t)(tok0 + (valid ? tok : 0)) * I, valid, blk0, nblk, t, xr);
+      staged_ai = c_ai;
+      staged_s = c_s;
+    }
+    float acc[4];
+    compute_item<NBW, kMulti>(L, xr, base, acc);
+    const int slot = ((i / B) & 1) * B + i % B;
+    stash<kMulti>(red, slot, warp, g, t, acc);
+    if (threadIdx.x == 0) s_meta[slot] = SlotMeta{tok0, n, c_rb * 16, c_s};
+    step(c_ai, c_s, c_rb);
+    if (i % B == B - 1 || i == my_items - 1) {
+      __syncthreads();
+      const int i0 = i - i % B, sl0 = ((i0 / B) & 1) * B;
+      const int jobs = (i - i0 + 1) * 16 * red_cols<kMulti>();
+      for (int job = threadIdx.x; job < jobs; job += kThreadsK) {
+        const int bi = job / (16 * red_cols<kMulti>()), rem = job % (16 * red_cols<kMulti>());
+        const int rr = rem & 15, tok = rem >> 4;
+        const SlotMeta m = s_meta[sl0 + bi];
+        if (tok >= m.n) continue;
+        const float ys = reduce_partials<kMulti>(red, sl0 + bi, rr, tok);
+        a.y_part[((int64_t)(m.tok0 + tok) * a.S + m.s) * H + m.row + rr] = ys;
+      }
+    }
+  };
+
+  issue(L0);
+  for (int i = 0; i < my_items; i += 2) {
+    if (i + 1 < my_items) issue(L1);
+    body(L0, i);
+    if (i + 1 >= my_items) break;
+    if (i + 2 < my_items) issue(L0);
+    body(L1, i + 1);
   }
 }
 
@@ -499,11 +548,15 @@ bool smem_attr(K kernel) {
          cudaSuccess;
 }
 
+template <bool kMulti, bool kFull>
+bool attrs_full() {
+  return smem_attr(k_gate_up_mma<1, kMulti, kFull>) && smem_attr(k_gate_up_mma<2, kMulti, kFull>) &&
+         smem_attr(k_gate_up_mma<4, kMulti, kFull>) && smem_attr(k_gate_up_mma<8, kMulti, kFull>) &&
+         smem_attr(k_down_mma<kDownSlice / (64 * kWarpsK), kMulti, kFull>);
+}
 template <bool kMulti>
 bool attrs() {
-  return smem_attr(k_gate_up_mma<1, kMulti>) && smem_attr(k_gate_up_mma<2, kMulti>) &&
-         smem_attr(k_gate_up_mma<4, kMulti>) && smem_attr(k_gate_up_mma<8, kMulti>) &&
-         smem_attr(k_down_mma<kDownSlice / (64 * kWarpsK), kMulti>);
+  return attrs_full<kMulti, true>() && attrs_full<kMulti, false>();
 }
 
 // Blocks per K part of the gate_up kernels: ceil(H / 64 / 16) rounded up to
@@ -513,14 +566,22 @@ int gate_nbw(int hidden) {
   return need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : -1;
 }
 
+template <int NBW, bool kMulti>
+void launch_gate_nbw(const DecodeArgs& a, cudaStream_t s) {
+  const int grid = sm_count();
+  if (a.H / 64 == NBW * kWarpsK)
+    k_gate_up_mma<NBW, kMulti, true><<<grid, kThreadsK, kDynSmem, s>>>(a);
+  else
+    k_gate_up_mma<NBW, kMulti, false><<<grid, kThreadsK, kDynSmem, s>>>(a);
+}
+
 template <bool kMulti>
 int launch_gate(const DecodeArgs& a, cudaStream_t s) {
-  const int grid = sm_count();
   switch (gate_nbw(a.H)) {
-    case 1: k_gate_up_mma<1, kMulti><<<grid, kThreadsK, kDynSmem, s>>>(a); break;
-    case 2: k_gate_up_mma<2, kMulti><<<grid, kThreadsK, kDynSmem, s>>>(a); break;
-    case 4: k_gate_up_mma<4, kMulti><<<grid, kThreadsK, kDynSmem, s>>>(a); break;
-    case 8: k_gate_up_mma<8, kMulti><<<grid, kThreadsK, kDynSmem, s>>>(a); break;
+    case 1: launch_gate_nbw<1, kMulti>(a, s); break;
+    case 2: launch_gate_nbw<2, kMulti>(a, s); break;
+    case 4: launch_gate_nbw<4, kMulti>(a, s); break;
+    case 8: launch_gate_nbw<8, kMulti>(a, s); break;
     default: return MOE_ERR_UNSUPPORTED;
   }
   MOE_CHECK_LAUNCH();
@@ -529,7 +590,11 @@ int launch_gate(const DecodeArgs& a, cudaStream_t s) {
 
 template <bool kMulti>
 int launch_down(const DecodeArgs& a, cudaStream_t s) {
-  k_down_mma<kDownSlice / (64 * kWarpsK), kMulti><<<sm_count(), kThreadsK, kDynSmem, s>>>(a);
+  constexpr int NBW = kDownSlice / (64 * kWarpsK);
+  if ((a.I / 64) % (kDownSlice / 64) == 0)
+    k_down_mma<NBW, kMulti, true><<<sm_count(), kThreadsK, kDynSmem, s>>>(a);
+  else
+    k_down_mma<NBW, kMulti, false><<<sm_count(), kThreadsK, kDynSmem, s>>>(a);
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
