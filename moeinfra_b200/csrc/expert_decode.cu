@@ -57,14 +57,17 @@ struct DecodeArgs {
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+// The decode table is written once, before a barrier, and only read after it;
+// the table reads and the MMAs are pure (non-volatile asm) so the compiler may
+// interleave the blocks' table reads with the MMA chains.
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
   uint32_t v;
-  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  asm("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
 __device__ __forceinline__ float2 lds64f(uint32_t addr) {
   float2 v;
-  asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+  asm("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
   return v;
 }
 __device__ __forceinline__ uint2 ldg_stream64(const uint8_t* p) {
@@ -104,7 +107,7 @@ __device__ __forceinline__ uint32_t decode(uint32_t w, uint32_t base, float absm
 
 __device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -254,7 +257,9 @@ __device__ __forceinline__ void stash(float* red, int slot, int warp, int g, int
       p[g * C + 2 * t + c] = acc[c];
       p[(g + 8) * C + 2 * t + c] = acc[2 + c];
     }
-  } else if (t == 0) {
+  } else {
+    // One token: every column of the MMA carries it, so the four t-lanes of a
+    // row hold the same sum; all write it (same word, same value).
     p[g] = acc[0];
     p[g + 8] = acc[2];
   }
@@ -373,7 +378,7 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_gate_up_mma(const __grid_const
     compute_item<NBW, kMulti>(L, xr, base, acc);
     const int slot = ((i / B) & 1) * B + i % B;
     stash<kMulti>(red, slot, warp, g, t, acc);
-    if (threadIdx.x == 0) s_meta[slot] = SlotMeta{tok0, n, (cp.r >> 1) * 16 + (cp.r & 1) * 8, 0};
+    if (warp == 0) s_meta[slot] = SlotMeta{tok0, n, (cp.r >> 1) * 16 + (cp.r & 1) * 8, 0};
     cp.next(per);
     if (i % B == B - 1 || i == my_items - 1) {
       __syncthreads();
@@ -493,7 +498,7 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_down_mma(const __grid_constant
     compute_item<NBW, kMulti>(L, xr, base, acc);
     const int slot = ((i / B) & 1) * B + i % B;
     stash<kMulti>(red, slot, warp, g, t, acc);
-    if (threadIdx.x == 0) s_meta[slot] = SlotMeta{tok0, n, c_rb * 16, c_s};
+    if (warp == 0) s_meta[slot] = SlotMeta{tok0, n, c_rb * 16, c_s};
     step(c_ai, c_s, c_rb);
     if (i % B == B - 1 || i == my_items - 1) {
       __syncthreads();
