@@ -193,6 +193,20 @@ def test_expert_forward_mixtral_shape(n):
     print(f"mixtral expert n={n}: rel_l2={r:.2e} max_abs={m:.2e}")
 
 
+@pytest.mark.parametrize("H,I", [(2048, 2048), (2048, 4096), (4096, 2048)])
+def test_expert_forward_ring_shapes(H, I):
+    """1-token experts whose K extents are whole 2048-element chunks take the
+    shared-memory ring kernels (both gate_up variants and down)."""
+    from moeinfra_b200 import _native
+
+    ex = make_experts(40 + H // 1024 + I // 512, 1, H, I, std=0.03)[0]
+    x = np.random.default_rng(H + I).standard_normal((1, H), dtype=np.float32).astype(np.float16)
+    for _ in range(2):
+        y = gpu_expert(ex, H, I)(_t(x)).cpu().numpy()
+        assert_close_fp16(y, onf4.expert_forward(x, ex, H, I), what=f"ring H={H} I={I}")
+    assert _native.take_device_error() == 0
+
+
 # ---------------------------------------------------------------------------
 # Fused layer
 # ---------------------------------------------------------------------------
@@ -217,6 +231,23 @@ def test_layer_forward_small(T):
     ref, ridx, rw, _ = omoe.moe_layer_forward(h, wg, experts, H, I, k)
     assert np.array_equal(idx.cpu().numpy(), ridx)
     assert_close_fp16(out.cpu().numpy(), ref, what=f"layer T={T}")
+
+
+@pytest.mark.parametrize("T", [1, 2, 5])
+def test_layer_forward_ring_mixed(T):
+    """Chunk-aligned shapes: 1-token experts on the GEMV kernels, 2..8-token
+    experts on the multi-token kernels, in one layer."""
+    from moeinfra_b200 import _native, kernels
+
+    H, I, E, k = 2048, 4096, 4, 2
+    h, wg, experts = _layer_case(T, H, I, E, k, seed=60 + T, gate_std=0.05)
+    gx = [gpu_expert(ex, H, I) for ex in experts]
+    table = kernels.expert_array([g.nf4_descriptor for g in gx])
+    out, idx, w = kernels.layer_forward(_t(h), _t(wg), table, k, H, I)
+    ref, ridx, rw, _ = omoe.moe_layer_forward(h, wg, experts, H, I, k)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    assert_close_fp16(out.cpu().numpy(), ref, what=f"ring layer T={T}")
+    assert _native.take_device_error() == 0
 
 
 def test_layer_forward_mixtral_bs1():
