@@ -194,16 +194,15 @@ def test_expert_forward_mixtral_shape(n):
 
 
 @pytest.mark.parametrize("H,I", [(2048, 2048), (2048, 4096), (4096, 2048)])
-def test_expert_forward_ring_shapes(H, I):
-    """1-token experts whose K extents are whole 2048-element chunks take the
-    shared-memory ring kernels (both gate_up variants and down)."""
+def test_expert_forward_chunk_aligned_shapes(H, I):
+    """1-token experts at other sizes whose K extents are whole 2048-element chunks."""
     from moeinfra_b200 import _native
 
     ex = make_experts(40 + H // 1024 + I // 512, 1, H, I, std=0.03)[0]
     x = np.random.default_rng(H + I).standard_normal((1, H), dtype=np.float32).astype(np.float16)
     for _ in range(2):
         y = gpu_expert(ex, H, I)(_t(x)).cpu().numpy()
-        assert_close_fp16(y, onf4.expert_forward(x, ex, H, I), what=f"ring H={H} I={I}")
+        assert_close_fp16(y, onf4.expert_forward(x, ex, H, I), what=f"expert H={H} I={I}")
     assert _native.take_device_error() == 0
 
 
@@ -234,7 +233,7 @@ def test_layer_forward_small(T):
 
 
 @pytest.mark.parametrize("T", [1, 2, 5])
-def test_layer_forward_ring_mixed(T):
+def test_layer_forward_chunk_aligned_mixed(T):
     """Chunk-aligned shapes: 1-token experts on the GEMV kernels, 2..8-token
     experts on the multi-token kernels, in one layer."""
     from moeinfra_b200 import _native, kernels
@@ -246,7 +245,7 @@ def test_layer_forward_ring_mixed(T):
     out, idx, w = kernels.layer_forward(_t(h), _t(wg), table, k, H, I)
     ref, ridx, rw, _ = omoe.moe_layer_forward(h, wg, experts, H, I, k)
     assert np.array_equal(idx.cpu().numpy(), ridx)
-    assert_close_fp16(out.cpu().numpy(), ref, what=f"ring layer T={T}")
+    assert_close_fp16(out.cpu().numpy(), ref, what=f"layer 2048x4096 T={T}")
     assert _native.take_device_error() == 0
 
 
