@@ -1,9 +1,509 @@
-// Grouped NF4 expert GEMM (tcgen05) -- placeholder until the kernel lands.
+// Grouped NF4 expert GEMM on the 5th-generation tensor cores (tcgen05 + TMEM),
+// for experts with more than 8 tokens (prefill and large decode batches).
+//
+// Reference: ReconstructedNF4Expert.forward (transfer/nf4_reconstruct.py:152-155)
+// on n > 1 tokens, where bitsandbytes dequantizes each NF4 weight to bf16
+// (nf4_reconstruct.py:12) and casts it to the fp16 compute dtype (:94) before an
+// fp16 GEMM with fp32 accumulation:  w = fp16(bf16(code * absmax)).
+//
+// One launch per projection; a persistent CTA per SM walks tiles of
+// (expert, 128 weight rows, up to 256 tokens of that expert):
+//   gate_up: D1 = W1 . X^T and D3 = W3 . X^T in TMEM (2 x 256 fp32 columns),
+//            epilogue h = fp16(silu(fp16(D1)) * fp16(D3)) -> h_sorted [P, I];
+//   down   : D = W2 . H^T (256 columns), epilogue y = fp16(D) -> y_sorted [P, H].
+// Warp roles (320 threads):
+//   warps 0-7  dequantize the 128 x 64 weight tile of each K step (one NF4
+//              block per row; warp w takes rows 32*(w%4).., byte half w/4)
+//              straight into shared memory in the UMMA K-major 128-byte
+//              swizzled layout, then run the epilogue (TMEM -> registers ->
+//              global);
+//   warp 8     lane 0 loads the token tile of each K step with TMA (no
+//              multicast; rows past the tensor read as zeros);
+//   warp 9     lane 0 issues tcgen05.mma (kind::f16, M = 128, N = tokens
+//              rounded up to 16, K = 16 per instruction) and commits stages.
+// Stage barriers: a_full (8 dequant warps), b_full (TMA bytes), empty (MMA
+// commit); accumulator barriers acc_full (MMA commit) and acc_empty (8
+// epilogue warps).  Every wait is bounded: on timeout the GEMM error word is
+// set, the waiting role stops, and before exit the CTA waits (bounded) for its
+// issued copies and MMAs, then frees its TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace moe {
-int launch_grouped_gemm_experts(const moe_nf4_expert_t*, int, const int32_t*, const uint16_t*,
-                                int64_t, int, int, uint16_t*, uint16_t*, cudaStream_t) {
-  return MOE_ERR_UNSUPPORTED;
+namespace {
+
+constexpr int kBM = 128;           // weight rows per tile (UMMA M)
+constexpr int kBK = 64;            // K per stage: one NF4 block
+constexpr int kMaxN = 256;         // tokens per tile (UMMA N, max)
+constexpr int kBoxRows = 64;       // token rows per TMA box
+constexpr int kDqWarps = 8;
+constexpr int kThreads = (kDqWarps + 2) * 32;
+constexpr uint32_t kATile = kBM * kBK * 2;         // 16 KB fp16, swizzled
+constexpr uint32_t kBBox = kBoxRows * kBK * 2;      // 8 KB
+constexpr uint32_t kBTile = kMaxN * kBK * 2;        // 32 KB
+constexpr uint32_t kLutBytes = 256 * 16 * 8;        // byte -> (code hi, code lo), 16 replicas
+constexpr long long kWaitCycles = 4000000000LL;     // ~2 s at 2 GHz
+
+__device__ int g_gemm_error = 0;
+
+template <bool kGate>
+struct Cfg {
+  static constexpr int kMats = kGate ? 2 : 1;
+  static constexpr int kStages = kGate ? 3 : 4;
+  static constexpr uint32_t kStage = kMats * kATile + kBTile;
+  static constexpr uint32_t kTmemCols = kGate ? 512 : 256;
+  static constexpr uint32_t kSmem = kStages * kStage + kLutBytes + 1024;  // + alignment slack
+};
+
+struct GemmArgs {
+  ExpertTable ex;
+  int E;
+  const int32_t* offsets;  // [E+1] rows of each expert in the token matrix
+  int K;                   // reduction length (H for gate_up, I for down)
+  int rows;                // output rows per expert (I for gate_up, H for down)
+  uint16_t* out;           // [P, rows] fp16
+};
+
+// ---- PTX wrappers ----------------------------------------------------------
+
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase of `parity`; false (error word set) after ~kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicExch(&g_gemm_error, 1);
+      return false;
+    }
+  }
+  return true;
+}
+// Warp-uniform wait: lane 0 waits, the result is broadcast (all lanes of a
+// warp then take the same path through warp-collective tcgen05 instructions).
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+// 2-D TMA load of one box into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+// D[tmem] (+)= A[smem desc] . B[smem desc]^T, kind::f16 (fp16 x fp16 -> fp32).
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (rows are 128 bytes = 64 fp16 of K).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor: fp32 accumulate, fp16 A and B, both K-major, M=128, N.
+__device__ __forceinline__ uint32_t instr_desc(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+// Tile t of this launch -> expert e, first weight row m0, first token n0, tokens nt.
+struct Tile {
+  int e, m0, n0, nt;
+};
+__device__ __forceinline__ Tile tile_of(int t, const int* s_base, const int* s_off, int E,
+                                        int mtiles) {
+  int e = 0;
+  while (e + 1 < E && s_base[e + 1] <= t) ++e;
+  const int local = t - s_base[e];
+  const int n_e = s_off[e + 1] - s_off[e];
+  const int nch = (n_e + kMaxN - 1) / kMaxN;
+  const int m = local / nch, c = local - m * nch;
+  const int n0 = c * kMaxN;
+  const int nt = min(kMaxN, n_e - n0);
+  return Tile{e, m * kBM, n0, nt};
+}
+
+template <bool kGate>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_grouped_gemm(const __grid_constant__ GemmArgs a, const __grid_constant__ CUtensorMap tmap) {
+  using C = Cfg<kGate>;
+  constexpr int NS = C::kStages;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ __align__(8) unsigned long long s_afull[NS], s_bfull[NS], s_empty[NS];
+  __shared__ __align__(8) unsigned long long s_accfull, s_accempty, s_drain;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_off[MOE_MAX_EXPERTS + 1];
+  __shared__ int s_base[MOE_MAX_EXPERTS + 1];
+  __shared__ float s_code[16];
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t raw = saddr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // stages: 1024-aligned (swizzle atoms)
+  const uint32_t lut = base + NS * C::kStage;
+  const int mtiles = a.rows / kBM;
+  const int nblk = a.K / kBK;
+
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e <= a.E; ++e) s_off[e] = a.offsets[e];
+    for (int e = 0; e < a.E; ++e) {
+      s_base[e] = acc;
+      const int n = s_off[e + 1] - s_off[e];
+      acc += n > 0 ? mtiles * ((n + kMaxN - 1) / kMaxN) : 0;
+    }
+    s_base[a.E] = acc;
+    s_abort = 0;
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(saddr(&s_afull[s]), kDqWarps);
+      mbar_init(saddr(&s_bfull[s]), 1);
+      mbar_init(saddr(&s_empty[s]), 1);
+    }
+    mbar_init(saddr(&s_accfull), 1);
+    mbar_init(saddr(&s_accempty), kDqWarps);
+    mbar_init(saddr(&s_drain), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (threadIdx.x < 16) s_code[threadIdx.x] = (kGate ? a.ex.e[0].w1.code : a.ex.e[0].w2.code)[threadIdx.x];
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(&s_tmem)),
+                 "r"(C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  // Byte -> (fp32 code of the high nibble, of the low nibble); 16 replicas so
+  // the 16 lanes of a half-warp read disjoint banks.
+  for (int i = threadIdx.x; i < 256 * 16; i += kThreads) {
+    const int v = i >> 4;
+    float2 c = make_float2(s_code[v >> 4], s_code[v & 15]);
+    asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(lut + i * 8), "f"(c.x), "f"(c.y)
+                 : "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  const int total = s_base[a.E];
+
+  if (warp < kDqWarps) {
+    // ---------------- dequant producers + epilogue ----------------
+    const int half = warp / 4, rw = warp % 4;
+    const int i = rw * 32 + lane;  // tile row (also TMEM lane)
+    const uint32_t lut_lane = lut + (lane & 15) * 8;
+    uint32_t g = 0, it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+      const Tile tl = tile_of(t, s_base, s_off, a.E, mtiles);
+      const moe_nf4_expert_t& ex = a.ex.e[tl.e];
+      const moe_nf4_matrix_t* mats[2] = {kGate ? &ex.w1 : &ex.w2, &ex.w3};
+      const int R = tl.m0 + i;
+      const int64_t rowseg = (int64_t)(R >> 4) * nblk * 16 + (R & 15);
+      bool stop = false;
+      for (int kb = 0; kb < nblk; ++kb, ++g) {
+        const int s = g % NS;
+        stop = __shfl_sync(0xffffffffu, s_abort, 0) != 0 ||
+               !warp_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1);
+        if (stop) {
+          s_abort = 1;
+          break;
+        }
+        const uint32_t stage = base + s * C::kStage;
+#pragma unroll
+        for (int m = 0; m < C::kMats; ++m) {
+          const int64_t seg = rowseg + (int64_t)kb * 16;
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(mats[m]->q + seg * 32 + half * 16));
+          const float am = __ldg(mats[m]->absmax + seg);
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+          const uint32_t arow = stage + m * kATile + (i >> 3) * 1024 + (i & 7) * 128;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t h[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const uint32_t v = (w[cc] >> (8 * b)) & 0xFFu;
+              float2 c;
+              asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(c.x), "=f"(c.y) : "r"(lut_lane + v * 128));
+              h[b] = nf4_pair_multirow(c.x, c.y, am);
+            }
+            const int chunk = half * 4 + cc;
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                             arow + ((chunk ^ (i & 7)) << 4)),
+                         "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
+                         : "memory");
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(saddr(&s_afull[s]));
+      }
+      if (stop) break;
+      // Epilogue: this warp reads TMEM lanes 32*rw.. ; column chunks of 16,
+      // alternating between the two byte halves' warps.
+      if (!warp_wait(saddr(&s_accfull), it & 1)) {
+        s_abort = 1;
+        break;
+      }
+      tc_fence_after();
+      const int nchunk = (tl.nt + 15) / 16;
+      const uint32_t lane_addr = tmem + ((uint32_t)(rw * 32) << 16);
+      for (int ch = half; ch < nchunk; ch += 2) {
+        uint32_t d1[16], d3[16];
+        tmem_ld16(lane_addr + ch * 16, d1);
+        if (kGate) tmem_ld16(lane_addr + 256 + ch * 16, d3);
+        tmem_wait_ld();
+        const int row = tl.m0 + i;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = ch * 16 + j;
+          if (n < tl.nt) {
+            const int64_t p = s_off[tl.e] + tl.n0 + n;
+            uint16_t o;
+            if (kGate)
+              o = swiglu_f16(f2h(__uint_as_float(d1[j])), f2h(__uint_as_float(d3[j])));
+            else
+              o = f2h(__uint_as_float(d1[j]));
+            a.out[p * a.rows + row] = o;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(saddr(&s_accempty));
+    }
+  } else if (warp == kDqWarps) {
+    // ---------------- TMA producer of the token tiles ----------------
+    if (lane == 0) {
+      uint32_t g = 0;
+      for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x) {
+        const Tile tl = tile_of(t, s_base, s_off, a.E, mtiles);
+        const int nbox = (tl.nt + kBoxRows - 1) / kBoxRows;
+        const int row0 = s_off[tl.e] + tl.n0;
+        for (int kb = 0; kb < nblk; ++kb, ++g) {
+          const int s = g % NS;
+          if (!s_abort && !mbar_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1)) s_abort = 1;
+          if (s_abort) break;
+          const uint32_t bar = saddr(&s_bfull[s]);
+          const uint32_t bt = base + s * C::kStage + C::kMats * kATile;
+          mbar_expect_tx(bar, nbox * kBBox);
+          for (int bx = 0; bx < nbox; ++bx)
+            tma_load_2d(bt + bx * kBBox, &tmap, bar, kb * kBK, row0 + bx * kBoxRows);
+        }
+      }
+      // Copies issued into stages never consumed (timeout): let them land.
+      if (s_abort)
+        for (uint32_t j = g > (uint32_t)NS ? g - NS : 0; j < g; ++j)
+          mbar_wait(saddr(&s_bfull[j % NS]), (j / NS) & 1);
+    }
+  } else {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t g = 0, it = 0;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x, ++it) {
+        const Tile tl = tile_of(t, s_base, s_off, a.E, mtiles);
+        const int n = (tl.nt + 15) & ~15;
+        const uint32_t idesc = instr_desc(n);
+        if (!mbar_wait(saddr(&s_accempty), (it & 1) ^ 1)) {
+          s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < nblk; ++kb, ++g) {
+          const int s = g % NS;
+          if (!mbar_wait(saddr(&s_afull[s]), (g / NS) & 1) ||
+              !mbar_wait(saddr(&s_bfull[s]), (g / NS) & 1)) {
+            s_abort = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t stage = base + s * C::kStage;
+          const uint32_t bt = stage + C::kMats * kATile;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+#pragma unroll
+            for (int m = 0; m < C::kMats; ++m)
+              tc_mma(tmem + m * 256, smem_desc(stage + m * kATile + kk * 32), smem_desc(bt + kk * 32),
+                     idesc, (kb | kk) != 0);
+          }
+          issued_any = true;
+          tc_commit(saddr(&s_empty[s]));
+        }
+        if (s_abort) break;
+        tc_commit(saddr(&s_accfull));
+      }
+      // After a timeout, wait (bounded) for the MMAs already issued.
+      if (s_abort && issued_any) {
+        tc_commit(saddr(&s_drain));
+        mbar_wait(saddr(&s_drain), 0);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(C::kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---- host side ----------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Token matrix [rows_total, K] fp16, row-major: boxes of 64 rows x 64 K with
+// the 128-byte swizzle the UMMA K-major descriptor expects.
+bool make_token_map(CUtensorMap* map, const uint16_t* x, int64_t rows_total, int K) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows_total};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {kBK, kBoxRows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool kGate>
+int launch_one(const GemmArgs& a, const uint16_t* x, int64_t P, cudaStream_t s) {
+  static bool attr = cudaFuncSetAttribute(k_grouped_gemm<kGate>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          Cfg<kGate>::kSmem) == cudaSuccess;
+  if (!attr) return MOE_ERR_CUDA;
+  CUtensorMap map;
+  if (!make_token_map(&map, x, P, a.K)) return MOE_ERR_CUDA;
+  k_grouped_gemm<kGate><<<sm_count(), kThreads, Cfg<kGate>::kSmem, s>>>(a, map);
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
+}  // namespace
+
+// Shapes the tensor-core path accepts: weight rows (I and H) multiples of 128,
+// K extents multiples of 64, K-major 16-byte-aligned operands.
+bool gemm_supported(int hidden, int inter) {
+  return hidden > 0 && inter > 0 && hidden % kBM == 0 && inter % kBM == 0 && hidden % kBK == 0 &&
+         inter % kBK == 0;
+}
+
+int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
+                                const int32_t* expert_offsets, const uint16_t* x_sorted,
+                                int64_t P, int hidden, int inter, uint16_t* h_sorted,
+                                uint16_t* y_sorted, cudaStream_t s) {
+  if (E < 1 || E > MOE_MAX_EXPERTS || P < 1) return MOE_ERR_INVALID_ARG;
+  if (!gemm_supported(hidden, inter)) return MOE_ERR_UNSUPPORTED;
+  if (P > INT32_MAX / 2) return MOE_ERR_UNSUPPORTED;
+  if (!aligned16(x_sorted) || !aligned16(h_sorted) || !aligned16(y_sorted))
+    return MOE_ERR_ALIGNMENT;
+  for (int e = 0; e < E; ++e) {
+    const moe_nf4_matrix_t* m[3] = {&experts[e].w1, &experts[e].w3, &experts[e].w2};
+    for (auto* mm : m)
+      if (!aligned16(mm->q) || (reinterpret_cast<uintptr_t>(mm->absmax) & 3)) return MOE_ERR_ALIGNMENT;
+  }
+  GemmArgs a{};
+  for (int e = 0; e < E; ++e) a.ex.e[e] = experts[e];
+  a.E = E;
+  a.offsets = expert_offsets;
+  a.K = hidden;
+  a.rows = inter;
+  a.out = h_sorted;
+  int st = launch_one<true>(a, x_sorted, P, s);
+  if (st != MOE_OK) return st;
+  a.K = inter;
+  a.rows = hidden;
+  a.out = y_sorted;
+  return launch_one<false>(a, h_sorted, P, s);
+}
+
+// Reads and clears the GEMM error word (a bounded barrier wait timed out).
+int gemm_take_error(int* value) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
+  *value = v;
+  return MOE_OK;
+}
+
 }  // namespace moe

@@ -206,6 +206,34 @@ def test_expert_forward_chunk_aligned_shapes(H, I):
     assert _native.take_device_error() == 0
 
 
+# Experts with more than 8 tokens run the tcgen05 grouped GEMM.
+@pytest.mark.parametrize("n", [9, 16, 100, 300])
+def test_expert_forward_gemm_small(n):
+    from moeinfra_b200 import _native
+
+    H, I = 256, 512
+    ex = make_experts(50 + n, 1, H, I, std=0.05)[0]
+    x = (np.random.default_rng(n).standard_normal((n, H), dtype=np.float32)).astype(np.float16)
+    g = gpu_expert(ex, H, I)
+    for _ in range(2):
+        y = g(_t(x)).cpu().numpy()
+        assert_close_fp16(y, onf4.expert_forward(x, ex, H, I), what=f"gemm expert n={n}")
+    assert _native.take_device_error() == 0
+
+
+@pytest.mark.parametrize("n", [16, 300])
+def test_expert_forward_gemm_mixtral_shape(n):
+    from moeinfra_b200 import _native
+
+    H, I = 4096, 14336
+    ex = make_experts(3, 1, H, I)[0]
+    x = np.random.default_rng(200 + n).standard_normal((n, H), dtype=np.float32).astype(np.float16)
+    y = gpu_expert(ex, H, I)(_t(x)).cpu().numpy()
+    r, m = assert_close_fp16(y, onf4.expert_forward(x, ex, H, I), what=f"gemm mixtral n={n}")
+    print(f"gemm mixtral expert n={n}: rel_l2={r:.2e} max_abs={m:.2e}")
+    assert _native.take_device_error() == 0
+
+
 # ---------------------------------------------------------------------------
 # Fused layer
 # ---------------------------------------------------------------------------
@@ -246,6 +274,22 @@ def test_layer_forward_chunk_aligned_mixed(T):
     ref, ridx, rw, _ = omoe.moe_layer_forward(h, wg, experts, H, I, k)
     assert np.array_equal(idx.cpu().numpy(), ridx)
     assert_close_fp16(out.cpu().numpy(), ref, what=f"layer 2048x4096 T={T}")
+    assert _native.take_device_error() == 0
+
+
+@pytest.mark.parametrize("T", [9, 64, 700])
+def test_layer_forward_gemm(T):
+    """Layers past 8 tokens: gather, tcgen05 grouped GEMM, ordered combine."""
+    from moeinfra_b200 import _native, kernels
+
+    H, I, E, k = 256, 512, 8, 2
+    h, wg, experts = _layer_case(T, H, I, E, k, seed=80 + T)
+    gx = [gpu_expert(ex, H, I) for ex in experts]
+    table = kernels.expert_array([g.nf4_descriptor for g in gx])
+    out, idx, w = kernels.layer_forward(_t(h), _t(wg), table, k, H, I)
+    ref, ridx, rw, _ = omoe.moe_layer_forward(h, wg, experts, H, I, k)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    assert_close_fp16(out.cpu().numpy(), ref, what=f"gemm layer T={T}")
     assert _native.take_device_error() == 0
 
 
