@@ -446,6 +446,8 @@ def run_device(args, rank: int, world: int, local_rank: int):
         line["hbm_gbs_step"] = round(routed_experts * EXPERT_BYTES / (ms / 1e3) / 1e9, 1)
         line["roofline"] = roof
         line["e2e"] = e2e
+        if not args.no_extra:
+            line.update(measure_batches(gates, tables, dev, L, K))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tps, per_layer, n, thr = cpu_layer_sample(steps=args.cpu_steps, warmup=1, batch=B,
                                                   time_budget_s=20.0)
@@ -457,6 +459,93 @@ def run_device(args, rank: int, world: int, local_rank: int):
     if graph is not None:
         del graph
     return line
+
+
+def _graph_time(fn, reps: int, dev) -> float:
+    """Mean ms of one replay of a CUDA graph of ``fn`` (captured after a warm-up call)."""
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = _events()
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    del g
+    return ms
+
+
+def measure_batches(gates, tables, dev, L: int, K: int):
+    """bs64 decode over the stack and config-2 prefill (4096 tokens per layer).
+
+    bs64: one step = 64 tokens through the L layers (CUDA graph), as the bs1 step.
+    prefill: 4096 N(0,1) tokens (seed 2) through one layer with an N(0,0.05) gate
+    (uneven expert loads), layers cycled; the expert stage (grouped tcgen05
+    GEMM) is also timed alone for its tensor-pipe roofline.
+    """
+    from moeinfra_b200 import kernels
+    out = {}
+    # --- bs64 decode ---
+    B = 64
+    toks = make_tokens(2, B, dev, rank=17)
+    h64 = toks[0].contiguous()
+    ms = _graph_time(lambda: [kernels.layer_forward(h64, gates[l], tables[l], TOP_K, HIDDEN, FFN)
+                              for l in range(L)], K, dev)
+    touched = 0
+    for l in range(L):
+        _, _, idx = kernels.router_topk(h64, gates[l], TOP_K, with_logits=False)
+        touched += len(set(idx.reshape(-1).tolist()))
+    out["bs64"] = {"value": round(B / (ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(ms, 4),
+                   "hbm_gbs": round(touched * EXPERT_BYTES / (ms / 1e3) / 1e9, 1),
+                   "experts_touched_per_step": touched,
+                   "note": "64 tokens through the stack per step (grouped tcgen05 GEMM path)"}
+    # --- prefill, config 2 ---
+    T = 4096
+    g = torch.Generator(device=dev).manual_seed(2)
+    xp = torch.randn(T, HIDDEN, generator=g, device=dev).to(torch.float16)
+    gates_pf = [(torch.randn(EXPERTS, HIDDEN, generator=g, device=dev) * 0.05).to(torch.float16)
+                for _ in range(min(L, 4))]
+    nl = len(gates_pf)
+
+    def prefill():
+        for l in range(nl):
+            kernels.layer_forward(xp, gates_pf[l], tables[l], TOP_K, HIDDEN, FFN)
+    reps = max(2, K // 4)
+    ms_pf = _graph_time(prefill, reps, dev) / nl
+    pairs = T * TOP_K
+    flops = pairs * 2 * 3 * HIDDEN * FFN
+    # expert stage alone (two grouped GEMM launches per layer)
+    stage_args = []
+    for l in range(nl):
+        _, w, idx = kernels.router_topk(xp, gates_pf[l], TOP_K, with_logits=False)
+        offsets, pair_token, _, _ = kernels.permute(idx, w, EXPERTS)
+        stage_args.append((offsets, kernels.gather_rows(xp, pair_token)))
+    ms_st = _graph_time(lambda: [kernels.experts_forward(tables[l], stage_args[l][0],
+                                                         stage_args[l][1], HIDDEN, FFN)
+                                 for l in range(nl)], reps, dev) / nl
+    peak = _measured_peak("bf16_tflops")
+    tflops = flops / (ms_st / 1e3) / 1e12
+    loads = torch.bincount(idx.reshape(-1), minlength=EXPERTS).tolist()
+    out["prefill"] = {"value": round(T / (ms_pf / 1e3), 1), "unit": "tok/s per layer",
+                      "ms_per_layer": round(ms_pf, 4), "tokens": T,
+                      "expert_loads_last_layer": loads,
+                      "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak[0],
+                                   "unit": "TFLOP/s", "frac": round(tflops / peak[0], 4),
+                                   "traffic": None,
+                                   "kernel": "grouped NF4 GEMM (gate_up + down launches), per layer",
+                                   "algorithmic_flop_per_launch": flops,
+                                   "launch_us": round(ms_st * 1e3, 1), "peak_source": peak[1]}}
+    return out
 
 
 def _measured_peak(key: str):
@@ -501,6 +590,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the bs64 and prefill measurements")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -39,6 +39,7 @@ constexpr int kBK = 64;            // K per stage: one NF4 block
 constexpr int kMaxN = 256;         // tokens per tile (UMMA N, max)
 constexpr int kBoxRows = 64;       // token rows per TMA box
 constexpr int kDqWarps = 8;
+constexpr int kPrefetch = 4;       // K steps of packed weights in flight per dequant thread
 constexpr int kThreads = (kDqWarps + 2) * 32;
 constexpr uint32_t kATile = kBM * kBK * 2;         // 16 KB fp16, swizzled
 constexpr uint32_t kBBox = kBoxRows * kBK * 2;      // 8 KB
@@ -264,43 +265,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       const moe_nf4_matrix_t* mats[2] = {kGate ? &ex.w1 : &ex.w2, &ex.w3};
       const int R = tl.m0 + i;
       const int64_t rowseg = (int64_t)(R >> 4) * nblk * 16 + (R & 15);
-      bool stop = false;
-      for (int kb = 0; kb < nblk; ++kb, ++g) {
-        const int s = g % NS;
-        stop = __shfl_sync(0xffffffffu, s_abort, 0) != 0 ||
-               !warp_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1);
-        if (stop) {
-          s_abort = 1;
-          break;
-        }
-        const uint32_t stage = base + s * C::kStage;
+      // Packed codes and absmax of K steps kb .. kb+kPrefetch-1 in flight in
+      // registers while step kb is decoded.
+      uint4 qv[kPrefetch][C::kMats];
+      float av[kPrefetch][C::kMats];
+      auto load = [&](int kb, uint4* q, float* am) {
+        if (kb < nblk) {
 #pragma unroll
-        for (int m = 0; m < C::kMats; ++m) {
-          const int64_t seg = rowseg + (int64_t)kb * 16;
-          const uint4 q = __ldg(reinterpret_cast<const uint4*>(mats[m]->q + seg * 32 + half * 16));
-          const float am = __ldg(mats[m]->absmax + seg);
-          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-          const uint32_t arow = stage + m * kATile + (i >> 3) * 1024 + (i & 7) * 128;
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            uint32_t h[4];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              const uint32_t v = (w[cc] >> (8 * b)) & 0xFFu;
-              float2 c;
-              asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(c.x), "=f"(c.y) : "r"(lut_lane + v * 128));
-              h[b] = nf4_pair_multirow(c.x, c.y, am);
-            }
-            const int chunk = half * 4 + cc;
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                             arow + ((chunk ^ (i & 7)) << 4)),
-                         "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
-                         : "memory");
+          for (int m = 0; m < C::kMats; ++m) {
+            const int64_t seg = rowseg + (int64_t)kb * 16;
+            q[m] = __ldg(reinterpret_cast<const uint4*>(mats[m]->q + seg * 32 + half * 16));
+            am[m] = __ldg(mats[m]->absmax + seg);
           }
         }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(saddr(&s_afull[s]));
+      };
+#pragma unroll
+      for (int d = 0; d < kPrefetch; ++d) load(d, qv[d], av[d]);
+      bool stop = false;
+      for (int kb0 = 0; kb0 < nblk && !stop; kb0 += kPrefetch) {
+#pragma unroll
+        for (int d = 0; d < kPrefetch; ++d) {
+          const int kb = kb0 + d;
+          if (kb >= nblk) break;
+          const int s = g % NS;
+          stop = __shfl_sync(0xffffffffu, s_abort, 0) != 0 ||
+                 !warp_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1);
+          if (stop) {
+            s_abort = 1;
+            break;
+          }
+          const uint32_t stage = base + s * C::kStage;
+#pragma unroll
+          for (int m = 0; m < C::kMats; ++m) {
+            const uint32_t w[4] = {qv[d][m].x, qv[d][m].y, qv[d][m].z, qv[d][m].w};
+            const float am = av[d][m];
+            const uint32_t arow = stage + m * kATile + (i >> 3) * 1024 + (i & 7) * 128;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              uint32_t h[4];
+#pragma unroll
+              for (int b = 0; b < 4; ++b) {
+                const uint32_t v = (w[cc] >> (8 * b)) & 0xFFu;
+                float2 c;
+                asm("ld.shared.v2.f32 {%0, %1}, [%2];"
+                    : "=f"(c.x), "=f"(c.y)
+                    : "r"(lut_lane + v * 128));
+                h[b] = nf4_pair_multirow(c.x, c.y, am);
+              }
+              const int chunk = half * 4 + cc;
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                               arow + ((chunk ^ (i & 7)) << 4)),
+                           "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
+                           : "memory");
+            }
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if ((threadIdx.x & 31) == 0) mbar_arrive(saddr(&s_afull[s]));
+          ++g;
+          load(kb + kPrefetch, qv[d], av[d]);
+        }
       }
       if (stop) break;
       // Epilogue: this warp reads TMEM lanes 32*rw.. ; column chunks of 16,
