@@ -75,13 +75,16 @@ __device__ __forceinline__ uint32_t saddr(const void* p) {
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
+// One try: the thread may be suspended in hardware (up to the hint, 10 ms)
+// until the phase completes, so a waiting thread takes no issue slots from
+// the warps sharing its scheduler.
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(10000000u)
       : "memory");
   return ok != 0;
 }
@@ -105,6 +108,27 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) {
   ok = __shfl_sync(0xffffffffu, ok, 0);
   __syncwarp();
   return ok != 0;
+}
+// Byte `shift/8` of w -> fp16 pair (element 2j low) of fp16(bf16(code * absmax)):
+// table address from the byte, the byte's two fp32 codes, one packed multiply,
+// bf16 rounding, then the exact widening to fp16 (the reference's multi-row
+// weight).  One PTX block so the sequence stays nine instructions.
+__device__ __forceinline__ uint32_t decode_byte(uint32_t w, uint32_t shift, uint32_t lut_lane,
+                                                uint64_t am2) {
+  uint32_t out;
+  asm("{\n .reg .b32 v, ad, lo, hi, bf;\n .reg .b64 c, p;\n"
+      " bfe.u32 v, %1, %2, 8;\n"
+      " mad.lo.u32 ad, v, 128, %3;\n"
+      " ld.shared.b64 c, [ad];\n"
+      " mul.rn.f32x2 p, c, %4;\n"
+      " mov.b64 {lo, hi}, p;\n"
+      " cvt.rn.bf16x2.f32 bf, hi, lo;\n"
+      " and.b32 hi, bf, 0xFFFF0000;\n"
+      " shl.b32 lo, bf, 16;\n"
+      " cvt.rn.f16x2.f32 %0, hi, lo;\n}\n"
+      : "=r"(out)
+      : "r"(w), "r"(shift), "r"(lut_lane), "l"(am2));
+  return out;
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
@@ -265,6 +289,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const moe_nf4_matrix_t* mats[2] = {kGate ? &ex.w1 : &ex.w2, &ex.w3};
       const int R = tl.m0 + i;
       const int64_t rowseg = (int64_t)(R >> 4) * nblk * 16 + (R & 15);
+      // This thread's 16 bytes of block 0 and its absmax; block kb is 512 bytes
+      // (16 floats) further on in tile16.
+      const uint4* qp[C::kMats];
+      const float* ap[C::kMats];
+#pragma unroll
+      for (int m = 0; m < C::kMats; ++m) {
+        qp[m] = reinterpret_cast<const uint4*>(mats[m]->q + rowseg * 32 + half * 16);
+        ap[m] = mats[m]->absmax + rowseg;
+      }
       // Packed codes and absmax of K steps kb .. kb+kPrefetch-1 in flight in
       // registers while step kb is decoded.
       uint4 qv[kPrefetch][C::kMats];
@@ -273,9 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kb < nblk) {
 #pragma unroll
           for (int m = 0; m < C::kMats; ++m) {
-            const int64_t seg = rowseg + (int64_t)kb * 16;
-            q[m] = __ldg(reinterpret_cast<const uint4*>(mats[m]->q + seg * 32 + half * 16));
-            am[m] = __ldg(mats[m]->absmax + seg);
+            q[m] = __ldg(qp[m] + (int64_t)kb * 32);
+            am[m] = __ldg(ap[m] + (int64_t)kb * 16);
           }
         }
       };
@@ -298,20 +330,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int m = 0; m < C::kMats; ++m) {
             const uint32_t w[4] = {qv[d][m].x, qv[d][m].y, qv[d][m].z, qv[d][m].w};
-            const float am = av[d][m];
+            const uint32_t amb = __float_as_uint(av[d][m]);
+            const uint64_t am2 = (static_cast<uint64_t>(amb) << 32) | amb;
             const uint32_t arow = stage + m * kATile + (i >> 3) * 1024 + (i & 7) * 128;
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
               uint32_t h[4];
 #pragma unroll
-              for (int b = 0; b < 4; ++b) {
-                const uint32_t v = (w[cc] >> (8 * b)) & 0xFFu;
-                float2 c;
-                asm("ld.shared.v2.f32 {%0, %1}, [%2];"
-                    : "=f"(c.x), "=f"(c.y)
-                    : "r"(lut_lane + v * 128));
-                h[b] = nf4_pair_multirow(c.x, c.y, am);
-              }
+              for (int b = 0; b < 4; ++b) h[b] = decode_byte(w[cc], 8 * b, lut_lane, am2);
               const int chunk = half * 4 + cc;
               asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
                                arow + ((chunk ^ (i & 7)) << 4)),
