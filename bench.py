@@ -309,16 +309,27 @@ def run_device(args, rank: int, world: int, local_rank: int):
             h_static.copy_(tokens[i])
             graph.replay()
     else:
+        # One eager step (creates the NCCL communicators and counts the
+        # library's kernels), then the whole step -- kernels and the NCCL
+        # all-to-alls of every layer -- captured in one CUDA graph.
         c0 = _native.launch_count()
         for lay in step_fn:
             lay(tokens[0])
         torch.cuda.synchronize()
         launches_per_step = _native.launch_count() - c0
+        h_static.copy_(tokens[0])
+        torch.cuda.synchronize()
+        _barrier(world)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for lay in step_fn:
+                lay(h_static)
+        torch.cuda.synchronize()
+        _barrier(world)
 
         def run(i):
-            x = tokens[i]
-            for lay in step_fn:
-                lay(x)
+            h_static.copy_(tokens[i])
+            graph.replay()
 
     for i in range(W):
         run(i)
@@ -457,6 +468,7 @@ def run_device(args, rank: int, world: int, local_rank: int):
                                           f"{per_layer:.3f} s per layer step), oracle.cpu_path "
                                           "torch CPU restatement"}
     if graph is not None:
+        graph.reset()  # a graph holding NCCL calls must go before the process group
         del graph
     return line
 
