@@ -240,21 +240,27 @@ int moe_combine(const uint16_t* y_sorted, const int32_t* pair_slot,
  * semantics (model/moe_layer.py:150-191) from tokens of every rank.
  *
  * moe_ep_dispatch (source; after moe_permute):
- *   send_rows fp16 [G*cap, hidden]: send_rows[r*cap+i] = h[pair_token[off[r*E/G]+i]]
- *   send_counts int32 [E] (tokens per expert, grouped by owner rank)
+ *   send_rows fp16 [G*(cap+1), hidden]: chunk r holds send_rows[r*(cap+1)+i] =
+ *   h[pair_token[off[r*E/G]+i]], and its last row (the header) carries rank r's
+ *   E/G expert counts as int32 in its first bytes, so one all-to-all of rows
+ *   also delivers the counts;
+ *   send_counts int32 [E] (optional, may be NULL): the same counts, compact;
  *   pair_slot_ep int32 [T*k]: row of pair t*k+j in the returned buffer
- * moe_ep_receive (owner; after the all-to-all of rows and counts):
+ * moe_ep_receive (owner; after the all-to-all of rows):
  *   x_sorted fp16 [G*cap, hidden] grouped by local expert (then source rank),
- *   local_offsets int32 [E/G + 1]; feed both to moe_experts_forward with P = G*cap.
- * moe_ep_return (owner): y_back[s*cap+i] = y_sorted[row of (s, i)]; after the
- *   all-to-all back, moe_combine(y_back, pair_slot_ep, ...) on the source.
- * Limits: E % G == 0, E <= 32, hidden % 8 == 0.
+ *   local_offsets int32 [E/G + 1], recv_counts int32 [E] (output: the counts
+ *   read from the headers, compact); feed x_sorted and local_offsets to
+ *   moe_experts_forward with P = G*cap.
+ * moe_ep_return (owner): y_back fp16 [G*cap, hidden]: y_back[s*cap+i] =
+ *   y_sorted[row of (s, i)], given the recv_counts moe_ep_receive wrote; after
+ *   the all-to-all back, moe_combine(y_back, pair_slot_ep, ...) on the source.
+ * Limits: E % G == 0, E <= 32, hidden % 8 == 0, 2*hidden >= 4*E/G.
  */
 int moe_ep_dispatch(const uint16_t* h, const int32_t* expert_offsets,
                     const int32_t* pair_token, const int32_t* pair_slot, int64_t T,
                     int k, int E, int G, int cap, int hidden, uint16_t* send_rows,
                     int32_t* send_counts, int32_t* pair_slot_ep, void* stream);
-int moe_ep_receive(const uint16_t* recv_rows, const int32_t* recv_counts, int E,
+int moe_ep_receive(const uint16_t* recv_rows, int32_t* recv_counts, int E,
                    int G, int cap, int hidden, uint16_t* x_sorted,
                    int32_t* local_offsets, void* stream);
 int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_counts, int E,

@@ -41,7 +41,14 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_dispatch(
   __syncthreads();
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  if (tid < E) send_counts[tid] = s_off[tid + 1] - s_off[tid];
+  // Header row (last row of each destination's chunk): that destination's El
+  // expert counts as int32 in its first bytes; the optional compact copy too.
+  if (tid < E) {
+    const int r = static_cast<int>(tid) / El, j = static_cast<int>(tid) - r * El;
+    const int c = s_off[tid + 1] - s_off[tid];
+    reinterpret_cast<int32_t*>(send + ((int64_t)r * (cap + 1) + cap) * vpr)[j] = c;
+    if (send_counts) send_counts[tid] = c;
+  }
   for (int64_t q = tid; q < P; q += stride) {
     const int p = pair_slot[q];
     int e = 0;
@@ -55,7 +62,8 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_dispatch(
     const int c = static_cast<int>(v - row * vpr);
     const int r = static_cast<int>(row / cap), i = static_cast<int>(row - (int64_t)r * cap);
     const int p = s_off[r * El] + i;
-    if (p < s_off[(r + 1) * El]) send[row * vpr + c] = h[(int64_t)pair_token[p] * vpr + c];
+    if (p < s_off[(r + 1) * El])
+      send[(row + r) * vpr + c] = h[(int64_t)pair_token[p] * vpr + c];  // chunk stride cap + 1
   }
 }
 
@@ -68,15 +76,16 @@ struct RecvPlan {
   int local_off[kEpMaxExperts + 1];
 };
 
-__device__ void build_plan(const int32_t* __restrict__ counts, int El, int G, int cap,
-                           RecvPlan& pl) {
+// counts of source s, local expert j at counts[s * stride + j].
+__device__ void build_plan(const int32_t* __restrict__ counts, int64_t stride, int El, int G,
+                           int cap, RecvPlan& pl) {
   if (threadIdx.x == 0) {
     // Counts come from peers; clamp so that no source exceeds its cap rows and
     // every derived row index stays inside the G*cap-row buffers.
     for (int s = 0; s < G; ++s) {
       int acc = 0;
       for (int j = 0; j < El; ++j) {
-        int c = counts[s * El + j];
+        int c = counts[s * stride + j];
         c = c < 0 ? 0 : (c > cap - acc ? cap - acc : c);
         pl.cnt[s * El + j] = c;
         pl.src_base[s * El + j] = acc;
@@ -105,14 +114,22 @@ __device__ __forceinline__ int64_t recv_dst(const RecvPlan& pl, int El, int s, i
   return pl.dst_base[s * El + j] + (i - pl.src_base[s * El + j]);
 }
 
+// kReceive: `in` is the received buffer (G chunks of cap + 1 rows, counts in
+// each chunk's header row); writes x_sorted, local offsets and the compact
+// counts.  Otherwise: `counts` is that compact copy and `in` is y_sorted.
 template <bool kReceive>
 __global__ void __launch_bounds__(kEpThreads) k_ep_move(
-    const uint4* __restrict__ in, const int32_t* __restrict__ counts, int El, int G, int cap,
+    const uint4* __restrict__ in, int32_t* __restrict__ counts, int El, int G, int cap,
     int vpr, uint4* __restrict__ out, int32_t* __restrict__ local_offsets) {
   __shared__ RecvPlan pl;
-  build_plan(counts, El, G, cap, pl);
+  if (kReceive)
+    build_plan(reinterpret_cast<const int32_t*>(in + (int64_t)cap * vpr),
+               (int64_t)(cap + 1) * vpr * 4, El, G, cap, pl);
+  else
+    build_plan(counts, El, El, G, cap, pl);
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (kReceive && tid <= El) local_offsets[tid] = pl.local_off[tid];
+  if (kReceive && tid < El * G) counts[tid] = pl.cnt[tid];
   const int64_t total = (int64_t)G * cap * vpr;
   const int64_t rows_out = (int64_t)G * cap;
   for (int64_t v = tid; v < total; v += (int64_t)gridDim.x * blockDim.x) {
@@ -122,15 +139,16 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_move(
     const int64_t dst = recv_dst(pl, El, s, i);
     if (dst < 0 || dst >= rows_out) continue;
     if (kReceive)
-      out[dst * vpr + c] = in[row * vpr + c];
+      out[dst * vpr + c] = in[(row + s) * vpr + c];  // chunk stride cap + 1
     else
       out[row * vpr + c] = in[dst * vpr + c];
   }
 }
 
+// The header row must hold E/G int32 counts: hidden * 2 >= 4 * E / G.
 bool ep_args_ok(int E, int G, int cap, int hidden) {
   return G >= 1 && E >= G && E <= kEpMaxExperts && E % G == 0 && cap >= 1 && hidden > 0 &&
-         hidden % 8 == 0;
+         hidden % 8 == 0 && hidden * 2 >= 4 * (E / G);
 }
 
 }  // namespace
@@ -144,7 +162,7 @@ extern "C" int moe_ep_dispatch(const uint16_t* h, const int32_t* expert_offsets,
   if (T < 0 || k < 1 || !ep_args_ok(E, G, cap, hidden)) return MOE_ERR_INVALID_ARG;
   const int El = E / G;
   if (T * (k < El ? k : El) > cap) return MOE_ERR_INVALID_ARG;
-  if (!expert_offsets || !send_counts || !send_rows) return MOE_ERR_INVALID_ARG;
+  if (!expert_offsets || !send_rows) return MOE_ERR_INVALID_ARG;
   if (T > 0 && (!h || !pair_token || !pair_slot || !pair_slot_ep)) return MOE_ERR_INVALID_ARG;
   if ((T > 0 && !aligned16(h)) || !aligned16(send_rows)) return MOE_ERR_ALIGNMENT;
   const int vpr = hidden / 8;
@@ -156,7 +174,7 @@ extern "C" int moe_ep_dispatch(const uint16_t* h, const int32_t* expert_offsets,
   return MOE_OK;
 }
 
-extern "C" int moe_ep_receive(const uint16_t* recv_rows, const int32_t* recv_counts, int E, int G,
+extern "C" int moe_ep_receive(const uint16_t* recv_rows, int32_t* recv_counts, int E, int G,
                               int cap, int hidden, uint16_t* x_sorted, int32_t* local_offsets,
                               void* stream) {
   using namespace moe;
@@ -181,7 +199,7 @@ extern "C" int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_count
   const int vpr = hidden / 8;
   k_ep_move<false><<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
                      static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint4*>(y_sorted), recv_counts, E / G, G, cap, vpr,
+      reinterpret_cast<const uint4*>(y_sorted), const_cast<int32_t*>(recv_counts), E / G, G, cap, vpr,
       reinterpret_cast<uint4*>(y_back), nullptr);
   MOE_CHECK_LAUNCH();
   return MOE_OK;

@@ -3,13 +3,14 @@
 Rank ``r`` of ``G`` owns experts ``[r*E/G, (r+1)*E/G)`` of every layer.  Each
 rank routes its own tokens; a layer step is
 
-    router -> permute -> ep_dispatch -> all_to_all(counts), all_to_all(rows)
-           -> ep_receive -> experts (local, grouped) -> ep_return
+    router -> permute -> ep_dispatch -> all_to_all(rows, with a count header
+           per rank) -> ep_receive -> experts (local, grouped) -> ep_return
            -> all_to_all(rows back) -> combine (ascending expert id)
 
 The exchanged buffers are capacity-padded (``cap = tokens * min(k, E/G)`` rows
-per rank pair), so every all-to-all has equal splits and no step reads a count
-back to the host: the step is a fixed sequence of kernels and NCCL calls.  Per
+per rank pair, plus one header row carrying the pair's expert counts), so the
+two all-to-alls have equal splits and no step reads a count back to the host:
+the step is a fixed sequence of kernels and two NCCL calls per layer.  Per
 token the result equals the single-GPU layer (``model/moe_layer.py:117-211``
 of the reference): each expert sees the same rows and the combine runs in the
 same order with the same roundings.
@@ -83,12 +84,10 @@ class ExpertParallelMoE:
         E, G, cap, k = self.num_experts, self.world, self.cap, self.top_k
         _, w, idx = kernels.router_topk(h, self.router.gate_f16(), k, with_logits=False)
         offsets, pair_token, _, pair_slot = kernels.permute(idx, w, E)
-        send, counts, slot_ep = kernels.ep_dispatch(h, offsets, pair_token, pair_slot, k, E, G, cap)
-        recv_counts = torch.empty_like(counts)
+        send, slot_ep = kernels.ep_dispatch(h, offsets, pair_token, pair_slot, k, E, G, cap)
         recv = torch.empty_like(send)
-        dist.all_to_all_single(recv_counts, counts, group=self.group)
-        dist.all_to_all_single(recv, send, group=self.group)
-        x_sorted, local_off = kernels.ep_receive(recv, recv_counts, E, G, cap)
+        dist.all_to_all_single(recv, send, group=self.group)  # rows + count headers
+        x_sorted, local_off, recv_counts = kernels.ep_receive(recv, E, G, cap)
         y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden, self.inter)
         y_back = kernels.ep_return(y_sorted, recv_counts, E, G, cap)
         y_home = torch.empty_like(y_back)

@@ -281,29 +281,32 @@ def combine(y_sorted: torch.Tensor, pair_slot: torch.Tensor, indices: torch.Tens
 
 def ep_dispatch(h: torch.Tensor, offsets: torch.Tensor, pair_token: torch.Tensor,
                 pair_slot: torch.Tensor, k: int, num_experts: int, world: int, cap: int):
-    """``(send_rows fp16 [world*cap, H], send_counts int32 [E], pair_slot_ep int32 [T*k])``."""
+    """``(send_rows fp16 [world*(cap+1), H], pair_slot_ep int32 [T*k])``.
+
+    Chunk r of ``send_rows`` is cap token rows for rank r followed by a header
+    row holding rank r's expert counts (int32).
+    """
     dev = _need_cuda("ep_dispatch", h=h, offsets=offsets)
     _need_dtype("ep_dispatch", h, torch.float16, "hidden_states")
     T, H = h.shape
-    send = torch.empty(world * cap, H, dtype=torch.float16, device=dev)
-    counts = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    send = torch.empty(world * (cap + 1), H, dtype=torch.float16, device=dev)
     slot_ep = torch.empty(T * k, dtype=torch.int32, device=dev)
     check(_native.lib().moe_ep_dispatch(_p(h), _p(offsets), _p(pair_token), _p(pair_slot), T, k,
-                                        num_experts, world, cap, H, _p(send), _p(counts),
+                                        num_experts, world, cap, H, _p(send), None,
                                         _p(slot_ep), _stream(dev)), "moe_ep_dispatch")
-    return send, counts, slot_ep
+    return send, slot_ep
 
 
-def ep_receive(recv_rows: torch.Tensor, recv_counts: torch.Tensor, num_experts: int, world: int,
-               cap: int):
-    """``(x_sorted fp16 [world*cap, H], local_offsets int32 [E/world + 1])``."""
-    dev = _need_cuda("ep_receive", recv_rows=recv_rows, recv_counts=recv_counts)
+def ep_receive(recv_rows: torch.Tensor, num_experts: int, world: int, cap: int):
+    """``(x_sorted fp16 [world*cap, H], local_offsets int32 [E/world + 1], recv_counts int32 [E])``."""
+    dev = _need_cuda("ep_receive", recv_rows=recv_rows)
     H = recv_rows.shape[1]
     x = torch.empty(world * cap, H, dtype=torch.float16, device=dev)
     off = torch.empty(num_experts // world + 1, dtype=torch.int32, device=dev)
-    check(_native.lib().moe_ep_receive(_p(recv_rows), _p(recv_counts), num_experts, world, cap, H,
+    counts = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    check(_native.lib().moe_ep_receive(_p(recv_rows), _p(counts), num_experts, world, cap, H,
                                        _p(x), _p(off), _stream(dev)), "moe_ep_receive")
-    return x, off
+    return x, off, counts
 
 
 def ep_return(y_sorted: torch.Tensor, recv_counts: torch.Tensor, num_experts: int, world: int,

@@ -8,7 +8,8 @@ exchange is restated here, step for step, with the layout the CUDA kernels
 
 * rank r of G owns experts [r*E/G, (r+1)*E/G);
 * source: rows sorted by expert (stable, ascending token), padded to ``cap``
-  rows per destination; counts per expert; ``pair_slot_ep`` addresses the
+  rows per destination, then a header row with that destination's expert
+  counts (one all-to-all carries both); ``pair_slot_ep`` addresses the
   returned rows;
 * owner: rows regrouped by (local expert, source rank, arrival order);
 * return: the inverse move, then the ordered combine of the reference.
@@ -35,20 +36,33 @@ def permute(idx: torch.Tensor, E: int):
 
 
 def dispatch(h: torch.Tensor, idx: torch.Tensor, E: int, G: int, cap: int):
-    """Source side: ``(send [G*cap, H], counts [E], pair_slot_ep [T*k])`` (padding rows zero)."""
+    """Source side: ``(send [G*(cap+1), H], counts [E], pair_slot_ep [T*k])``.
+
+    Chunk r is cap token rows (padding rows zero) and a header row whose first
+    E/G int32 are rank r's expert counts (rest zero).
+    """
     El = E // G
     offsets, pair_token, pair_slot = permute(idx, E)
     H = h.shape[1]
-    send = torch.zeros(G * cap, H, dtype=h.dtype)
+    send = torch.zeros(G * (cap + 1), H, dtype=h.dtype)
     for r in range(G):
         lo, hi = int(offsets[r * El]), int(offsets[(r + 1) * El])
         assert hi - lo <= cap
-        send[r * cap:r * cap + hi - lo] = h[pair_token[lo:hi]]
+        send[r * (cap + 1):r * (cap + 1) + hi - lo] = h[pair_token[lo:hi]]
     counts = (offsets[1:] - offsets[:-1]).to(torch.int32)
+    for r in range(G):
+        header = send[r * (cap + 1) + cap].view(torch.int32)
+        header[:El] = counts[r * El:(r + 1) * El]
     expert_of = torch.repeat_interleave(torch.arange(E), offsets[1:] - offsets[:-1])
     owner = expert_of[pair_slot] // El
     slot_ep = (owner * cap + pair_slot - offsets[owner * El]).to(torch.int32)
     return send, counts, slot_ep
+
+
+def header_counts(recv: torch.Tensor, E: int, G: int, cap: int) -> torch.Tensor:
+    """Compact counts [E] read from the header row of each source's chunk."""
+    El = E // G
+    return torch.cat([recv[s * (cap + 1) + cap].view(torch.int32)[:El] for s in range(G)])
 
 
 def receive_plan(recv_counts: torch.Tensor, E: int, G: int):
@@ -72,13 +86,15 @@ def receive_plan(recv_counts: torch.Tensor, E: int, G: int):
     return torch.tensor(local_off, dtype=torch.int32), dst
 
 
-def receive(recv: torch.Tensor, recv_counts: torch.Tensor, E: int, G: int, cap: int):
-    local_off, dst = receive_plan(recv_counts, E, G)
+def receive(recv: torch.Tensor, E: int, G: int, cap: int):
+    """``(x_sorted [G*cap, H], local_offsets [El+1], counts [E])`` from a received buffer."""
+    counts = header_counts(recv, E, G, cap)
+    local_off, dst = receive_plan(counts, E, G)
     x = torch.zeros(G * cap, recv.shape[1], dtype=recv.dtype)
     for s in range(G):
         for i, d in enumerate(dst[s]):
-            x[d] = recv[s * cap + i]
-    return x, local_off
+            x[d] = recv[s * (cap + 1) + i]
+    return x, local_off, counts
 
 
 def give_back(y_sorted: torch.Tensor, recv_counts: torch.Tensor, E: int, G: int, cap: int):

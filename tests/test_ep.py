@@ -97,11 +97,10 @@ def _gloo_worker(rank: int, world: int, port: int, cases: list):
             cap = ep.capacity(T, k, E, world)
             send, counts, slot_ep = oep.dispatch(torch.from_numpy(hs[rank]), torch.from_numpy(idx),
                                                  E, world, cap)
-            recv_counts = torch.empty_like(counts)
-            _a2a(recv_counts, counts)
             recv = torch.empty_like(send)
-            _a2a(recv, send)
-            x, local_off = oep.receive(recv, recv_counts, E, world, cap)
+            _a2a(recv, send)  # token rows and the count header of each chunk
+            x, local_off, recv_counts = oep.receive(recv, E, world, cap)
+            assert int(recv_counts.sum()) == int(local_off[-1])
             y_sorted = torch.zeros_like(x)
             for j, e in enumerate(ep.local_experts(rank, E, world)):
                 lo, hi = int(local_off[j]), int(local_off[j + 1])
@@ -149,21 +148,23 @@ def test_ep_kernels_emulated(G, T):
         h = torch.from_numpy(hs[s]).cuda()
         _, w, idx = kernels.router_topk(h, wg, k, with_logits=False)
         off, ptok, _, pslot = kernels.permute(idx, w, E)
-        send, counts, slot_ep = kernels.ep_dispatch(h, off, ptok, pslot, k, E, G, cap)
+        send, slot_ep = kernels.ep_dispatch(h, off, ptok, pslot, k, E, G, cap)
         o_send, o_counts, o_slot = oep.dispatch(torch.from_numpy(hs[s]), idx.cpu(), E, G, cap)
-        assert torch.equal(counts.cpu(), o_counts)
+        assert torch.equal(oep.header_counts(send.cpu(), E, G, cap), o_counts)
         assert torch.equal(slot_ep.cpu(), o_slot)
         for r in range(G):
             n = int(o_counts[r * El:(r + 1) * El].sum())
-            assert torch.equal(send[r * cap:r * cap + n].cpu().view(torch.int16),
-                               o_send[r * cap:r * cap + n].view(torch.int16))
-        src.append((h, w, idx, send, counts, slot_ep))
+            c0 = r * (cap + 1)
+            assert torch.equal(send[c0:c0 + n].cpu().view(torch.int16),
+                               o_send[c0:c0 + n].view(torch.int16))
+        src.append((h, w, idx, send, slot_ep))
     backs = []
+    C = cap + 1
     for r in range(G):
-        recv = torch.cat([src[s][3][r * cap:(r + 1) * cap] for s in range(G)])
-        recv_counts = torch.cat([src[s][4][r * El:(r + 1) * El] for s in range(G)])
-        x, local_off = kernels.ep_receive(recv, recv_counts, E, G, cap)
-        o_x, o_off = oep.receive(recv.cpu(), recv_counts.cpu(), E, G, cap)
+        recv = torch.cat([src[s][3][r * C:(r + 1) * C] for s in range(G)])
+        x, local_off, recv_counts = kernels.ep_receive(recv, E, G, cap)
+        o_x, o_off, o_counts = oep.receive(recv.cpu(), E, G, cap)
+        assert torch.equal(recv_counts.cpu(), o_counts)
         assert torch.equal(local_off.cpu(), o_off)
         n = int(o_off[-1])
         assert torch.equal(x[:n].cpu().view(torch.int16), o_x[:n].view(torch.int16))
@@ -178,7 +179,7 @@ def test_ep_kernels_emulated(G, T):
                                o_back[s * cap:s * cap + m].view(torch.int16))
         backs.append(y_back)
     for s in range(G):
-        h, w, idx, _, _, slot_ep = src[s]
+        h, w, idx, _, slot_ep = src[s]
         y_home = torch.cat([backs[r][s * cap:(s + 1) * cap] for r in range(G)])
         out = kernels.combine(y_home, slot_ep, idx, w)
         assert_close_fp16(out.cpu().numpy(), want[s], what=f"EP G={G} rank {s}")
