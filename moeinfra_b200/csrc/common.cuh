@@ -21,6 +21,34 @@
 namespace moe {
 void note_launch();
 
+// Programmatic dependent launch.  Kernels of one decode layer (router,
+// permute, expert GEMVs, combine) are launched with programmatic stream
+// serialization: a kernel may start while its predecessor still runs, so its
+// prologue (e.g. the decode table) overlaps the predecessor's tail.  Each such
+// kernel lets its successor launch (pdl_trigger) and, before it reads anything
+// an earlier kernel wrote -- and before it can finish -- waits for its
+// predecessor to complete (pdl_wait; a no-op when launched normally).
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 constexpr int kWarp = 32;
 
 // Expert descriptors passed by value as a kernel parameter.

@@ -307,10 +307,15 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_gate_up_mma(const __grid_const
   __shared__ SlotMeta s_meta[2 * B];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
+  // The decode table depends only on the weights' codebook (one per launch),
+  // so it is built before waiting for the kernel that produced the inputs.
+  pdl_trigger();
+  const bool lut_ok = smem_u32(smem) + red_floats<kMulti>() * 4 <= kLutWin &&
+                      build_lut(a.ex.e[0].w1.code, smem);
+  pdl_wait();
+  if (!lut_ok) return;
   const Active act = load_active<kMulti>(a, s_off, s_active);
   if (act.n == 0) return;
-  if (smem_u32(smem) + red_floats<kMulti>() * 4 > kLutWin) return;
-  if (!build_lut(a.ex.e[act.first].w1.code, smem)) return;
   float* red = reinterpret_cast<float*>(smem);
 
   const int H = a.H, I = a.I;
@@ -419,10 +424,15 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_down_mma(const __grid_constant
   __shared__ SlotMeta s_meta[2 * B];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
+  // The decode table depends only on the weights' codebook (one per launch),
+  // so it is built before waiting for the kernel that produced the inputs.
+  pdl_trigger();
+  const bool lut_ok = smem_u32(smem) + red_floats<kMulti>() * 4 <= kLutWin &&
+                      build_lut(a.ex.e[0].w2.code, smem);
+  pdl_wait();
+  if (!lut_ok) return;
   const Active act = load_active<kMulti>(a, s_off, s_active);
   if (act.n == 0) return;
-  if (smem_u32(smem) + red_floats<kMulti>() * 4 > kLutWin) return;
-  if (!build_lut(a.ex.e[act.first].w2.code, smem)) return;
   float* red = reinterpret_cast<float*>(smem);
 
   const int H = a.H, I = a.I;
@@ -528,6 +538,8 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_down_mma(const __grid_constant
 // y[slot] = fp16(sum over splits of y_part[slot][s]) (single-expert forward).
 __global__ void k_reduce_partials(const float* __restrict__ part, int64_t P, int S, int width,
                                   uint16_t* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t total = P * width;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -572,23 +584,27 @@ int gate_nbw(int hidden) {
 }
 
 template <int NBW, bool kMulti>
-void launch_gate_nbw(const DecodeArgs& a, cudaStream_t s) {
+cudaError_t launch_gate_nbw(const DecodeArgs& a, cudaStream_t s) {
   const int grid = sm_count();
+  cudaError_t st;
   if (a.H / 64 == NBW * kWarpsK)
-    k_gate_up_mma<NBW, kMulti, true><<<grid, kThreadsK, kDynSmem, s>>>(a);
+    st = launch_pdl(k_gate_up_mma<NBW, kMulti, true>, grid, kThreadsK, kDynSmem, s, a);
   else
-    k_gate_up_mma<NBW, kMulti, false><<<grid, kThreadsK, kDynSmem, s>>>(a);
+    st = launch_pdl(k_gate_up_mma<NBW, kMulti, false>, grid, kThreadsK, kDynSmem, s, a);
+  return st;
 }
 
 template <bool kMulti>
 int launch_gate(const DecodeArgs& a, cudaStream_t s) {
+  cudaError_t st;
   switch (gate_nbw(a.H)) {
-    case 1: launch_gate_nbw<1, kMulti>(a, s); break;
-    case 2: launch_gate_nbw<2, kMulti>(a, s); break;
-    case 4: launch_gate_nbw<4, kMulti>(a, s); break;
-    case 8: launch_gate_nbw<8, kMulti>(a, s); break;
+    case 1: st = launch_gate_nbw<1, kMulti>(a, s); break;
+    case 2: st = launch_gate_nbw<2, kMulti>(a, s); break;
+    case 4: st = launch_gate_nbw<4, kMulti>(a, s); break;
+    case 8: st = launch_gate_nbw<8, kMulti>(a, s); break;
     default: return MOE_ERR_UNSUPPORTED;
   }
+  if (st != cudaSuccess) return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
@@ -596,10 +612,12 @@ int launch_gate(const DecodeArgs& a, cudaStream_t s) {
 template <bool kMulti>
 int launch_down(const DecodeArgs& a, cudaStream_t s) {
   constexpr int NBW = kDownSlice / (64 * kWarpsK);
+  cudaError_t st;
   if ((a.I / 64) % (kDownSlice / 64) == 0)
-    k_down_mma<NBW, kMulti, true><<<sm_count(), kThreadsK, kDynSmem, s>>>(a);
+    st = launch_pdl(k_down_mma<NBW, kMulti, true>, sm_count(), kThreadsK, kDynSmem, s, a);
   else
-    k_down_mma<NBW, kMulti, false><<<sm_count(), kThreadsK, kDynSmem, s>>>(a);
+    st = launch_pdl(k_down_mma<NBW, kMulti, false>, sm_count(), kThreadsK, kDynSmem, s, a);
+  if (st != cudaSuccess) return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
@@ -647,7 +665,9 @@ int launch_reduce_partials(const float* part, int64_t P, int S, int width, uint1
                            cudaStream_t s) {
   int64_t blocks = ceil_div(P * width, 256);
   int grid = static_cast<int>(blocks < sm_count() * 8 ? blocks : sm_count() * 8);
-  k_reduce_partials<<<grid > 0 ? grid : 1, 256, 0, s>>>(part, P, S, width, y);
+  if (launch_pdl(k_reduce_partials, grid > 0 ? grid : 1, 256, 0, s, part, P, S, width, y) !=
+      cudaSuccess)
+    return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }

@@ -19,6 +19,8 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(
     const int64_t* __restrict__ indices, const float* __restrict__ weights, int64_t T, int k,
     int E, int32_t* __restrict__ expert_offsets, int32_t* __restrict__ pair_token,
     float* __restrict__ pair_weight, int32_t* __restrict__ pair_slot) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int s_count[32];
   __shared__ int s_off[33];
   __shared__ int s_run[32];
@@ -117,6 +119,8 @@ template <class Y>
 __global__ void k_combine(Y ysrc, const int32_t* __restrict__ pair_slot,
                           const int64_t* __restrict__ indices, const float* __restrict__ weights,
                           int64_t T, int k, int width, uint16_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t total = T * width;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -158,8 +162,9 @@ int grid_for(int64_t work, int threads) {
 int launch_combine_partials(const float* part, int S, const int32_t* pair_slot,
                             const int64_t* indices, const float* weights, int64_t T, int k,
                             int width, uint16_t* out, cudaStream_t s) {
-  k_combine<YPartials><<<grid_for(T * width, 256), 256, 0, s>>>(
-      YPartials{part, S}, pair_slot, indices, weights, T, k, width, out);
+  if (launch_pdl(k_combine<YPartials>, grid_for(T * width, 256), 256, 0, s, YPartials{part, S},
+                 pair_slot, indices, weights, T, k, width, out) != cudaSuccess)
+    return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
@@ -167,8 +172,9 @@ int launch_combine_partials(const float* part, int S, const int32_t* pair_slot,
 int launch_permute(const int64_t* indices, const float* weights, int64_t T, int k, int E,
                    int32_t* expert_offsets, int32_t* pair_token, float* pair_weight,
                    int32_t* pair_slot, cudaStream_t s) {
-  k_permute<<<1, kPermThreads, 0, s>>>(indices, weights, T, k, E, expert_offsets, pair_token,
-                                       pair_weight, pair_slot);
+  if (launch_pdl(k_permute, 1, kPermThreads, 0, s, indices, weights, T, k, E, expert_offsets,
+                 pair_token, pair_weight, pair_slot) != cudaSuccess)
+    return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }

@@ -160,6 +160,8 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(
     const uint4* __restrict__ h, const uint4* __restrict__ wg, int64_t T, int H, int E, int W,
     int k, uint16_t* __restrict__ logits, float* __restrict__ weights,
     int64_t* __restrict__ indices) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t t = blockIdx.x * (int64_t)kRouterWarps + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -186,6 +188,8 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk_cta(
     const uint4* __restrict__ h, const uint4* __restrict__ wg, int64_t T, int H, int E, int W,
     int k, uint16_t* __restrict__ logits, float* __restrict__ weights,
     int64_t* __restrict__ indices) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ FF s_part[kRouterWarps][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t t = blockIdx.x;
@@ -217,6 +221,8 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk_cta(
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router_from_logits(
     const uint16_t* __restrict__ logits, int64_t T, int E, int W, int k,
     float* __restrict__ weights, int64_t* __restrict__ indices) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t t = blockIdx.x * (int64_t)kRouterWarps + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -248,17 +254,19 @@ extern "C" int moe_router_topk(const uint16_t* h, const uint16_t* wg, int64_t T,
   const int W = next_pow2(E);
   // Code size matters (each token runs the unrolled body once): instantiate
   // for the expert-count bound that covers E.
+  cudaError_t st = cudaSuccess;
   if (T <= 2 * sm_count()) {
     const int grid = static_cast<int>(T);
-    if (E <= 8) k_router_topk_cta<8><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
-    else if (E <= 16) k_router_topk_cta<16><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
-    else k_router_topk_cta<32><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
+    if (E <= 8) st = launch_pdl(k_router_topk_cta<8>, grid, kRouterWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits, weights, indices);
+    else if (E <= 16) st = launch_pdl(k_router_topk_cta<16>, grid, kRouterWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits, weights, indices);
+    else st = launch_pdl(k_router_topk_cta<32>, grid, kRouterWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits, weights, indices);
   } else {
     const int grid = static_cast<int>(ceil_div(T, kRouterWarps));
-    if (E <= 8) k_router_topk<8><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
-    else if (E <= 16) k_router_topk<16><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
-    else k_router_topk<32><<<grid, kRouterWarps * 32, 0, s>>>(h4, w4, T, H, E, W, k, logits, weights, indices);
+    if (E <= 8) st = launch_pdl(k_router_topk<8>, grid, kRouterWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits, weights, indices);
+    else if (E <= 16) st = launch_pdl(k_router_topk<16>, grid, kRouterWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits, weights, indices);
+    else st = launch_pdl(k_router_topk<32>, grid, kRouterWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits, weights, indices);
   }
+  if (st != cudaSuccess) return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
@@ -270,8 +278,9 @@ extern "C" int moe_router_topk_from_logits(const uint16_t* logits, int64_t T, in
   if (T == 0) return MOE_OK;
   if (!logits || !weights || !indices) return MOE_ERR_INVALID_ARG;
   int grid = static_cast<int>(ceil_div(T, kRouterWarps));
-  k_router_from_logits<<<grid, kRouterWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+  cudaError_t st = launch_pdl(k_router_from_logits, grid, kRouterWarps * 32, 0, static_cast<cudaStream_t>(stream), 
       logits, T, E, next_pow2(E), k, weights, indices);
+  if (st != cudaSuccess) return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
