@@ -6,8 +6,8 @@
 //   w, idx = topk(p, k)                                              (:86-90)
 //   w /= w.sum(-1, keepdim=True)                                     (:92)
 //
-// Few tokens: one CTA per token (8 warps split H, so every load of the row is
-// in flight at once); many tokens: one warp per token.  Lane j (< E) owns
+// Few tokens: one CTA of 32 warps per token (warps split experts and H, so
+// every load of the row is in flight at once); many tokens: one warp per token.  Lane j (< E) owns
 // expert j after the dot-product reduction.  The softmax follows the operation order of torch's CUDA warp
 // softmax for a last dimension <= 32: butterfly max and butterfly sum over
 // next_pow2(E) lanes (offsets W/2 .. 1), exp(l - max), then e / sum, so the
@@ -181,37 +181,61 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(
   finish_token(mine, lane, E, W, k, t, logits, weights, indices);
 }
 
-// Few tokens: one CTA per token, the 8 warps split H; partial sums meet in
-// shared memory (fixed order) so every load of the row is in flight at once.
-template <int EMAX>
-__global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk_cta(
+// Few tokens: one CTA of 32 warps per token.  Warp w takes expert w % E and
+// range w / E of the row's 16-byte vectors (32 / E ranges), issues its loads
+// ahead of the arithmetic, and sums exactly in double-float; the ranges meet in
+// shared memory in a fixed order.  The fp16 logit is the correctly rounded sum,
+// as in the many-token kernel.
+constexpr int kCtaWarps = 32;
+constexpr int kCtaUnroll = 4;
+
+__global__ void __launch_bounds__(kCtaWarps * 32) k_router_topk_cta(
     const uint4* __restrict__ h, const uint4* __restrict__ wg, int64_t T, int H, int E, int W,
     int k, uint16_t* __restrict__ logits, float* __restrict__ weights,
     int64_t* __restrict__ indices) {
   pdl_trigger();
   pdl_wait();
-  __shared__ FF s_part[kRouterWarps][32];
+  __shared__ FF s_part[kCtaWarps];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t t = blockIdx.x;
   const int nvec = H >> 3;
-  FF acc[EMAX];
+  const int groups = kCtaWarps / E;  // >= 1 for E <= 32
+  if (warp < groups * E) {
+    const int e = warp % E, r = warp / E;
+    const int v0 = static_cast<int>((int64_t)nvec * r / groups);
+    const int v1 = static_cast<int>((int64_t)nvec * (r + 1) / groups);
+    const uint4* hrow = h + t * nvec;
+    const uint4* wrow = wg + (int64_t)e * nvec;
+    FF acc{0.f, 0.f};
+    for (int vb = v0 + lane; vb < v1; vb += 32 * kCtaUnroll) {
+      uint4 hv[kCtaUnroll], wv[kCtaUnroll];
 #pragma unroll
-  for (int e = 0; e < EMAX; ++e) acc[e] = FF{0.f, 0.f};
-  gate_dots<EMAX>(h + t * nvec, wg, nvec, E, threadIdx.x, kRouterWarps * 32, acc);
+      for (int u = 0; u < kCtaUnroll; ++u) {
+        const int v = vb + u * 32;
+        hv[u] = v < v1 ? hrow[v] : make_uint4(0, 0, 0, 0);
+        wv[u] = v < v1 ? __ldg(wrow + v) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-  for (int e = 0; e < EMAX; ++e) {
-    if (e < E) {
-      const FF s = warp_sum_ff(acc[e]);
-      if (lane == e) s_part[warp][e] = s;
+      for (int u = 0; u < kCtaUnroll; ++u) {
+        const __half2* hh = reinterpret_cast<const __half2*>(&hv[u]);
+        const __half2* ww = reinterpret_cast<const __half2*>(&wv[u]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 x = __half22float2(hh[q]), y = __half22float2(ww[q]);
+          ff_add(acc, __fmul_rn(x.x, y.x));
+          ff_add(acc, __fmul_rn(x.y, y.y));
+        }
+      }
     }
+    const FF tot = warp_sum_ff(acc);
+    if (lane == 0) s_part[warp] = tot;
   }
   __syncthreads();
   if (warp == 0) {
     double mine = 0.0;
     if (lane < E) {
-      FF tot = s_part[0][lane];
-#pragma unroll
-      for (int w = 1; w < kRouterWarps; ++w) ff_merge(tot, s_part[w][lane]);
+      FF tot = s_part[lane];
+      for (int r = 1; r < groups; ++r) ff_merge(tot, s_part[r * E + lane]);
       mine = ff_value(tot);
     }
     finish_token(mine, lane, E, W, k, t, logits, weights, indices);
@@ -257,9 +281,8 @@ extern "C" int moe_router_topk(const uint16_t* h, const uint16_t* wg, int64_t T,
   cudaError_t st = cudaSuccess;
   if (T <= 2 * sm_count()) {
     const int grid = static_cast<int>(T);
-    if (E <= 8) st = launch_pdl(k_router_topk_cta<8>, grid, kRouterWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits, weights, indices);
-    else if (E <= 16) st = launch_pdl(k_router_topk_cta<16>, grid, kRouterWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits, weights, indices);
-    else st = launch_pdl(k_router_topk_cta<32>, grid, kRouterWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits, weights, indices);
+    st = launch_pdl(k_router_topk_cta, grid, kCtaWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits,
+                    weights, indices);
   } else {
     const int grid = static_cast<int>(ceil_div(T, kRouterWarps));
     if (E <= 8) st = launch_pdl(k_router_topk<8>, grid, kRouterWarps * 32, 0, s, h4, w4, T, H, E, W, k, logits, weights, indices);
