@@ -612,9 +612,19 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
+    # stdout carries only the JSON line: libraries that print banners (NCCL's
+    # version line on rank 0) write to file descriptor 1, so it goes to stderr
+    # for the whole run and the result is written to the saved descriptor.
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+
+    def emit(line: dict) -> None:
+        os.write(json_fd, (json.dumps(line) + "\n").encode())
+
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args)), flush=True)
+            emit(run_reference(args))
         return 0
 
     if world > 1:
@@ -625,7 +635,7 @@ def main():
     try:
         line = run_device(args, rank, world, local_rank)
         if rank == 0:
-            print(json.dumps(line), flush=True)
+            emit(line)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()
