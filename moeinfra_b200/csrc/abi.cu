@@ -36,17 +36,20 @@ __device__ int g_wait_error = 0;
 }  // namespace moe
 
 namespace moe {
-int gemm_take_error(int* value);  // expert_gemm_sm100.cu
+int gemm_take_error(int* value);    // expert_gemm_sm100.cu
+int decode_take_error(int* value);  // expert_decode.cu
 }
 
 extern "C" int moe_take_device_error(int* value) {
   if (!value) return MOE_ERR_INVALID_ARG;
   int gemm = 0;
   if (moe::gemm_take_error(&gemm) != MOE_OK) return MOE_ERR_CUDA;
+  int decode = 0;
+  if (moe::decode_take_error(&decode) != MOE_OK) return MOE_ERR_CUDA;
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, moe::g_wait_error, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
   const int zero = 0;
   if (cudaMemcpyToSymbol(moe::g_wait_error, &zero, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
-  *value = v | gemm;
+  *value = v | gemm | decode;
   return MOE_OK;
 }

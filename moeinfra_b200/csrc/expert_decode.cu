@@ -51,6 +51,7 @@ struct DecodeArgs {
   const uint16_t* x;              // fp16 input rows [*, H]
   uint16_t* h_sorted;             // fp16 [P, I]
   float* y_part;                  // fp32 [P][S][H]
+  int* sync;                      // [MOE_MAX_EXPERTS][S] gate_up completion counters, zeroed
   int H, I, S;
 };
 
@@ -175,8 +176,9 @@ __device__ __forceinline__ Active load_active(const DecodeArgs& a, int* s_off, i
 
 // x words of this thread for blocks [blk0, blk0+NBW): elements blk*64+16t..+16
 // of the token its B column carries (zeros past the expert's token count or
-// past the row's last block).
-template <int NBW>
+// past the row's last block).  kL2: rows written by other CTAs of the same
+// launch, read through L2.
+template <int NBW, bool kL2>
 __device__ __forceinline__ void load_x(const uint16_t* row, bool valid, int blk0, int blk_end,
                                        int t, uint32_t (*xr)[8]) {
 #pragma unroll
@@ -184,8 +186,13 @@ __device__ __forceinline__ void load_x(const uint16_t* row, bool valid, int blk0
     uint4 u0 = make_uint4(0, 0, 0, 0), u1 = u0;
     if (valid && blk0 + kb < blk_end) {
       const uint4* p = reinterpret_cast<const uint4*>(row + (blk0 + kb) * 64 + 16 * t);
-      u0 = p[0];
-      u1 = p[1];
+      if (kL2) {
+        u0 = __ldcg(p);
+        u1 = __ldcg(p + 1);
+      } else {
+        u0 = p[0];
+        u1 = p[1];
+      }
     }
     xr[kb][0] = u0.x; xr[kb][1] = u0.y; xr[kb][2] = u0.z; xr[kb][3] = u0.w;
     xr[kb][4] = u1.x; xr[kb][5] = u1.y; xr[kb][6] = u1.z; xr[kb][7] = u1.w;
@@ -198,8 +205,15 @@ template <bool kMulti>
 constexpr int batch_items() { return kMulti ? 2 : 8; }
 template <bool kMulti>
 constexpr int red_cols() { return kMulti ? kMaxTok : 1; }
+// Row tiles (16 rows) per down item: two for 1-token experts (an item then
+// moves as many weight bytes as a gate_up item), one for 2..8 tokens (whose
+// partials take 8 columns).
 template <bool kMulti>
-constexpr int red_floats() { return 2 * batch_items<kMulti>() * kWarpsK * 16 * red_cols<kMulti>(); }
+constexpr int down_tiles() { return kMulti ? 1 : 2; }
+template <bool kMulti>
+constexpr int red_floats() {
+  return 2 * batch_items<kMulti>() * kWarpsK * 16 * down_tiles<kMulti>() * red_cols<kMulti>();
+}
 
 // Register-resident loads of one item: MMA rows g (qa, sa) and g+8 (qb, sb),
 // blocks kb of this warp's K part.
@@ -247,10 +261,13 @@ __device__ __forceinline__ void compute_item(const ItemLoads<NBW>& L, const uint
   }
 }
 
-template <bool kMulti>
-__device__ __forceinline__ void stash(float* red, int slot, int warp, int g, int t, const float* acc) {
+// Partials of (slot, warp) take R rows x C columns; this MMA tile's rows
+// start at row0.
+template <bool kMulti, int R>
+__device__ __forceinline__ void stash(float* red, int slot, int warp, int g, int t, const float* acc,
+                                      int row0) {
   constexpr int C = red_cols<kMulti>();
-  float* p = red + ((slot * kWarpsK + warp) * 16) * C;
+  float* p = red + ((slot * kWarpsK + warp) * R + row0) * C;
   if (kMulti) {
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
@@ -266,17 +283,17 @@ __device__ __forceinline__ void stash(float* red, int slot, int warp, int g, int
 }
 
 // Sum of the 16 warp partials (warp order) of (slot, row, column).
-template <bool kMulti>
+template <bool kMulti, int R>
 __device__ __forceinline__ float reduce_partials(const float* red, int slot, int row, int col) {
   constexpr int C = red_cols<kMulti>();
-  const float* p = red + (slot * kWarpsK * 16 + row) * C + col;
+  const float* p = red + (slot * kWarpsK * R + row) * C + col;
   float s = p[0];
 #pragma unroll
-  for (int w = 1; w < kWarpsK; ++w) s = __fadd_rn(s, p[w * 16 * C]);
+  for (int w = 1; w < kWarpsK; ++w) s = __fadd_rn(s, p[w * R * C]);
   return s;
 }
 
-// Where a reduced item goes (written by thread 0 before the batch barrier).
+// Where a reduced item goes (written by warp 0 before the batch barrier).
 struct SlotMeta {
   int tok0;  // first sorted pair of the item's expert
   int n;     // tokens of that expert
@@ -296,28 +313,82 @@ struct Cursor {
   }
 };
 
-// gate_up.  NBW = 64-element blocks per warp (16 warps split H).  Item = 8 rows
-// of W1 and the same 8 rows of W3 (one MMA), r = 2*tile + half.
+// ---------------------------------------------------------------------------
+// Cross-CTA hand-off between the two phases of one launch.
+//
+// a.sync[ai * S + s] counts the gate_up items of active expert ai whose rows
+// fall in down split s and whose h rows are written.  A CTA publishes its
+// items once, after the barrier that follows its last stores (barrier, then
+// one thread: release fence, atomic adds); a fence per batch would wait on
+// the ring's loads in flight.  The down phase acquires the counter
+// before it reads the split's h rows, which it reads through L2 (ld.cg).
+// The counters are zeroed by the kernel that runs before each launch on the
+// stream (permute / offsets) or by a memset.
+constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
+
+__device__ int g_decode_error = 0;
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until *p >= target; on timeout records the error and returns
+// (the launch's results are then invalid, the host reads the error word).
+__device__ __forceinline__ void wait_count(const int* p, int target) {
+  if (ld_acquire(p) >= target) return;
+  const long long t0 = clock64();
+  while (ld_acquire(p) < target) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicOr(&g_decode_error, 1);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
+// Release fence of the publishing thread (orders the CTA's stores, made
+// visible to it by the preceding barrier, before the counter update).
+__device__ __forceinline__ void fence_release_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+// Adds the gate_up items [first, last) (per items per active expert, 256 per
+// down split) to their (expert, split) counters.
+__device__ __forceinline__ void publish_items(int* sync, int first, int last, int per, int S) {
+  constexpr int kItemsPerSplit = kDownSlice / 8;
+  fence_release_gpu();
+  int i = first;
+  while (i < last) {
+    const int ai = i / per, r = i - ai * per;
+    const int s = r / kItemsPerSplit;
+    const int end = min(last, ai * per + min(per, (s + 1) * kItemsPerSplit));
+    atomicAdd(sync + ai * S + s, end - i);
+    i = end;
+  }
+}
+
+// gate_up items of down split s (8 rows each).
+__device__ __forceinline__ int split_items(int I, int s) {
+  return min(kDownSlice, I - s * kDownSlice) / 8;
+}
+
+struct StageSmem {
+  float* red;
+  const int* s_off;
+  const int* s_active;
+  SlotMeta* s_meta;
+};
+
+// gate_up phase.  NBW = 64-element blocks per warp (16 warps split H).  Item =
+// 8 rows of W1 and the same 8 rows of W3 (one MMA), r = 2*tile + half.
 template <int NBW, bool kMulti, bool kFull>
-__global__ void __launch_bounds__(kThreadsK, 1) k_gate_up_mma(const __grid_constant__ DecodeArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ int s_off[MOE_MAX_EXPERTS + 1];
-  __shared__ int s_active[MOE_MAX_EXPERTS];
+__device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& act,
+                                           const StageSmem& sm) {
   constexpr int B = batch_items<kMulti>();
-  __shared__ SlotMeta s_meta[2 * B];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  // The decode table depends only on the weights' codebook (one per launch),
-  // so it is built before waiting for the kernel that produced the inputs.
-  pdl_trigger();
-  const bool lut_ok = smem_u32(smem) + red_floats<kMulti>() * 4 <= kLutWin &&
-                      build_lut(a.ex.e[0].w1.code, smem);
-  pdl_wait();
-  if (!lut_ok) return;
-  const Active act = load_active<kMulti>(a, s_off, s_active);
-  if (act.n == 0) return;
-  float* red = reinterpret_cast<float*>(smem);
-
   const int H = a.H, I = a.I;
   const int nblk = H / 64;
   const int per = I / 8;
@@ -325,6 +396,10 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_gate_up_mma(const __grid_const
   cta_range(act.n * per, &first, &last);
   const int my_items = last - first;
   if (my_items <= 0) return;
+  float* red = sm.red;
+  const int* s_off = sm.s_off;
+  const int* s_active = sm.s_active;
+  SlotMeta* s_meta = sm.s_meta;
   const uint32_t base = kMulti ? (kLutWin | 128u | ((lane & 15) * 8)) : (kLutWin | (lane * 4));
   const int blk0 = warp * NBW;
   const int kb_valid = nblk - blk0;  // blocks of this warp inside the row
@@ -376,13 +451,13 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_gate_up_mma(const __grid_const
       const bool valid = tok < n;
       const int64_t xrow =
           valid ? (a.pair_token ? a.pair_token[tok0 + tok] : (int64_t)(tok0 + tok)) : 0;
-      load_x<NBW>(a.x + xrow * H, valid, blk0, nblk, t, xr);
+      load_x<NBW, false>(a.x + xrow * H, valid, blk0, nblk, t, xr);
       staged = cp.ai;
     }
     float acc[4];
     compute_item<NBW, kMulti>(L, xr, base, acc);
     const int slot = ((i / B) & 1) * B + i % B;
-    stash<kMulti>(red, slot, warp, g, t, acc);
+    stash<kMulti, 16>(red, slot, warp, g, t, acc, 0);
     if (warp == 0) s_meta[slot] = SlotMeta{tok0, n, (cp.r >> 1) * 16 + (cp.r & 1) * 8, 0};
     cp.next(per);
     if (i % B == B - 1 || i == my_items - 1) {
@@ -395,9 +470,144 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_gate_up_mma(const __grid_const
         const int rr = rem & 7, tok = rem >> 3;
         const SlotMeta m = s_meta[sl0 + bi];
         if (tok >= m.n) continue;
-        const float gs = reduce_partials<kMulti>(red, sl0 + bi, rr, tok);
-        const float us = reduce_partials<kMulti>(red, sl0 + bi, rr + 8, tok);
+        const float gs = reduce_partials<kMulti, 16>(red, sl0 + bi, rr, tok);
+        const float us = reduce_partials<kMulti, 16>(red, sl0 + bi, rr + 8, tok);
         a.h_sorted[(int64_t)(m.tok0 + tok) * I + m.row + rr] = swiglu_f16(f2h(gs), f2h(us));
+      }
+    }
+  };
+
+  issue(L0);
+  for (int i = 0; i < my_items; i += 2) {
+    if (i + 1 < my_items) issue(L1);
+    body(L0, i);
+    if (i + 1 >= my_items) break;
+    if (i + 2 < my_items) issue(L0);
+    body(L1, i + 1);
+  }
+  // Every h store of this CTA, and every warp's reads of the partial slots,
+  // are done after this barrier; then the CTA's items are published per
+  // (expert, split) counter.
+  __syncthreads();
+  if (threadIdx.x == 0) publish_items(a.sync, first, last, per, a.S);
+}
+
+// down phase.  NBW = 64-element blocks per warp of one 2048-element split.
+// Item = (split s, group rg of kT consecutive 16-row W2 tiles), rg fastest:
+// r = s * groups + rg.
+template <int NBW, bool kMulti, bool kFull>
+__device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& act,
+                                           const StageSmem& sm) {
+  constexpr int B = batch_items<kMulti>();
+  constexpr int kT = down_tiles<kMulti>();
+  constexpr int kRows = 16 * kT;
+  constexpr int C = red_cols<kMulti>();
+  constexpr int kSplitBlocks = kDownSlice / 64;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int H = a.H, I = a.I;
+  const int nblk = I / 64;
+  const int groups = H / kRows;
+  const int per = a.S * groups;
+  int first, last;
+  cta_range(act.n * per, &first, &last);
+  const int my_items = last - first;
+  if (my_items <= 0) return;
+  float* red = sm.red;
+  const int* s_off = sm.s_off;
+  const int* s_active = sm.s_active;
+  SlotMeta* s_meta = sm.s_meta;
+  const uint32_t base = kMulti ? (kLutWin | 128u | ((lane & 15) * 8)) : (kLutWin | (lane * 4));
+  const int wblk = warp * NBW;  // this warp's first block within a split
+  const int64_t tile_q = (int64_t)nblk * 512, tile_s = (int64_t)nblk * 16;
+  const int thr_q = wblk * 512 + g * 32 + t * 8, thr_s = wblk * 16 + g;
+
+  uint32_t xr[NBW][8];
+  ItemLoads<NBW> L0[kT], L1[kT];
+  // (ai, s, rg) of the next item to load / compute.
+  int l_ai = first / per, l_r = first % per;
+  int l_s = l_r / groups, l_rg = l_r % groups;
+  int c_ai = l_ai, c_s = l_s, c_rg = l_rg;
+  const moe_nf4_expert_t* ld_ex = &a.ex.e[s_active[l_ai]];
+  int staged_ai = -1, staged_s = -1;
+  auto step = [&](int& ai, int& s, int& rg) {
+    if (++rg == groups) {
+      rg = 0;
+      if (++s == a.S) {
+        s = 0;
+        ++ai;
+      }
+    }
+  };
+
+  auto issue = [&](ItemLoads<NBW>* L) {
+    const int64_t qo = (int64_t)l_rg * kT * tile_q + (int64_t)l_s * kSplitBlocks * 512 + thr_q;
+    const int64_t so = (int64_t)l_rg * kT * tile_s + (int64_t)l_s * kSplitBlocks * 16 + thr_s;
+    const uint8_t* q = ld_ex->w2.q + qo;
+    const float* sc = ld_ex->w2.absmax + so;
+    const int kb_valid = nblk - l_s * kSplitBlocks - wblk;
+#pragma unroll
+    for (int tt = 0; tt < kT; ++tt)
+      load_item<NBW, kFull>(L[tt], q + tt * tile_q, q + tt * tile_q + 256, sc + tt * tile_s,
+                            sc + tt * tile_s + 8, kb_valid);
+    const int ai = l_ai;
+    step(l_ai, l_s, l_rg);
+    if (l_ai != ai && l_ai < act.n) ld_ex = &a.ex.e[s_active[l_ai]];
+  };
+  // One thread pulls an upcoming item's blocks (contiguous in tile16) into L2.
+  int p_ai = c_ai, p_s = c_s, p_rg = c_rg;
+  auto prefetch = [&]() {
+    if (p_ai < act.n) {
+      const moe_nf4_expert_t& ex = a.ex.e[s_active[p_ai]];
+      const int b0 = p_s * kSplitBlocks, b1 = min(b0 + kSplitBlocks, nblk);
+#pragma unroll
+      for (int tt = 0; tt < kT; ++tt) {
+        const int64_t seg0 = ((int64_t)(p_rg * kT + tt) * nblk + b0) * 16;
+        prefetch_l2(ex.w2.q + seg0 * 32, (uint32_t)(b1 - b0) * 512u);
+        prefetch_l2(ex.w2.absmax + seg0, (uint32_t)(b1 - b0) * 64u);
+      }
+    }
+    step(p_ai, p_s, p_rg);
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kPrefetchItems; ++i) prefetch();
+
+  auto body = [&](const ItemLoads<NBW>* L, int i) {
+    if (threadIdx.x == 0) prefetch();
+    const int e = s_active[c_ai];
+    const int tok0 = s_off[e];
+    const int n = s_off[e + 1] - tok0;
+    if (c_ai != staged_ai || c_s != staged_s) {
+      // h rows of this split come from other CTAs' gate_up items.
+      wait_count(a.sync + c_ai * a.S + c_s, split_items(I, c_s));
+      const int blk0 = c_s * kSplitBlocks + wblk;
+      const int tok = kMulti ? g : 0;
+      const bool valid = tok < n;
+      load_x<NBW, true>(a.h_sorted + (int64_t)(tok0 + (valid ? tok : 0)) * I, valid, blk0, nblk, t,
+                        xr);
+      staged_ai = c_ai;
+      staged_s = c_s;
+    }
+    const int slot = ((i / B) & 1) * B + i % B;
+#pragma unroll
+    for (int tt = 0; tt < kT; ++tt) {
+      float acc[4];
+      compute_item<NBW, kMulti>(L[tt], xr, base, acc);
+      stash<kMulti, kRows>(red, slot, warp, g, t, acc, tt * 16);
+    }
+    if (warp == 0) s_meta[slot] = SlotMeta{tok0, n, c_rg * kRows, c_s};
+    step(c_ai, c_s, c_rg);
+    if (i % B == B - 1 || i == my_items - 1) {
+      __syncthreads();
+      const int i0 = i - i % B, sl0 = ((i0 / B) & 1) * B;
+      const int jobs = (i - i0 + 1) * kRows * C;
+      for (int job = threadIdx.x; job < jobs; job += kThreadsK) {
+        const int bi = job / (kRows * C), rem = job % (kRows * C);
+        const int rr = rem % kRows, tok = rem / kRows;
+        const SlotMeta m = s_meta[sl0 + bi];
+        if (tok >= m.n) continue;
+        const float ys = reduce_partials<kMulti, kRows>(red, sl0 + bi, rr, tok);
+        a.y_part[((int64_t)(m.tok0 + tok) * a.S + m.s) * H + m.row + rr] = ys;
       }
     }
   };
@@ -412,127 +622,45 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_gate_up_mma(const __grid_const
   }
 }
 
-// down.  NBW = 64-element blocks per warp of one 2048-element split.  Item =
-// (split s, tile rb of 16 W2 rows), rb fastest: r = s * tiles + rb.
-template <int NBW, bool kMulti, bool kFull>
-__global__ void __launch_bounds__(kThreadsK, 1) k_down_mma(const __grid_constant__ DecodeArgs a) {
+__device__ __forceinline__ bool same_codebook(const float* a, const float* b) {
+  if (a == b) return true;
+  bool same = true;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) same &= __ldg(a + i) == __ldg(b + i);
+  return same;
+}
+
+// One launch per layer for the experts of one kind (1 token or 2..8 tokens):
+// every CTA runs its share of the gate_up items, then its share of the down
+// items; a down split starts as soon as the gate_up items it reads are
+// published, with its weight loads and L2 prefetches already in flight.  The
+// grid is one CTA per SM and every gate_up item is done before its CTA waits
+// on anything, so the waits end once all CTAs are resident.
+template <int NBW, bool kMulti, bool kFullG, bool kFullD>
+__global__ void __launch_bounds__(kThreadsK, 1) k_stage_mma(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_off[MOE_MAX_EXPERTS + 1];
   __shared__ int s_active[MOE_MAX_EXPERTS];
-  constexpr int B = batch_items<kMulti>();
-  constexpr int kSplitBlocks = kDownSlice / 64;
-  __shared__ SlotMeta s_meta[2 * B];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  // The decode table depends only on the weights' codebook (one per launch),
-  // so it is built before waiting for the kernel that produced the inputs.
+  __shared__ SlotMeta s_meta[2 * batch_items<kMulti>()];
+  // The decode table depends only on the weights' codebook (one per launch).
+  // The 1-token launch, first in a layer, builds it before waiting for the
+  // kernel that produced its inputs; the 2..8-token launch follows a
+  // full-grid kernel (nothing to overlap) and first checks it has work.
   pdl_trigger();
-  const bool lut_ok = smem_u32(smem) + red_floats<kMulti>() * 4 <= kLutWin &&
-                      build_lut(a.ex.e[0].w2.code, smem);
+  const bool room = smem_u32(smem) + red_floats<kMulti>() * 4 <= kLutWin;
+  bool lut_ok = !kMulti && room && build_lut(a.ex.e[0].w1.code, smem);
   pdl_wait();
-  if (!lut_ok) return;
   const Active act = load_active<kMulti>(a, s_off, s_active);
   if (act.n == 0) return;
-  float* red = reinterpret_cast<float*>(smem);
-
-  const int H = a.H, I = a.I;
-  const int nblk = I / 64;
-  const int tiles = H / 16;
-  const int per = a.S * tiles;
-  int first, last;
-  cta_range(act.n * per, &first, &last);
-  const int my_items = last - first;
-  if (my_items <= 0) return;
-  const uint32_t base = kMulti ? (kLutWin | 128u | ((lane & 15) * 8)) : (kLutWin | (lane * 4));
-  const int wblk = warp * NBW;  // this warp's first block within a split
-  const int64_t tile_q = (int64_t)nblk * 512, tile_s = (int64_t)nblk * 16;
-  const int thr_q = wblk * 512 + g * 32 + t * 8, thr_s = wblk * 16 + g;
-
-  uint32_t xr[NBW][8];
-  ItemLoads<NBW> L0, L1;
-  // (ai, s, rb) of the next item to load / compute.
-  int l_ai = first / per, l_r = first % per;
-  int l_s = l_r / tiles, l_rb = l_r % tiles;
-  int c_ai = l_ai, c_s = l_s, c_rb = l_rb;
-  const moe_nf4_expert_t* ld_ex = &a.ex.e[s_active[l_ai]];
-  int staged_ai = -1, staged_s = -1;
-  auto step = [&](int& ai, int& s, int& rb) {
-    if (++rb == tiles) {
-      rb = 0;
-      if (++s == a.S) {
-        s = 0;
-        ++ai;
-      }
-    }
-  };
-
-  auto issue = [&](ItemLoads<NBW>& L) {
-    const int64_t qo = l_rb * tile_q + (int64_t)l_s * kSplitBlocks * 512 + thr_q;
-    const int64_t so = l_rb * tile_s + (int64_t)l_s * kSplitBlocks * 16 + thr_s;
-    const uint8_t* q = ld_ex->w2.q + qo;
-    const float* sc = ld_ex->w2.absmax + so;
-    load_item<NBW, kFull>(L, q, q + 256, sc, sc + 8, nblk - l_s * kSplitBlocks - wblk);
-    const int ai = l_ai;
-    step(l_ai, l_s, l_rb);
-    if (l_ai != ai && l_ai < act.n) ld_ex = &a.ex.e[s_active[l_ai]];
-  };
-  // One thread pulls an upcoming item's blocks (contiguous in tile16) into L2.
-  int p_ai = c_ai, p_s = c_s, p_rb = c_rb;
-  auto prefetch = [&]() {
-    if (p_ai < act.n) {
-      const moe_nf4_expert_t& ex = a.ex.e[s_active[p_ai]];
-      const int b0 = p_s * kSplitBlocks, b1 = min(b0 + kSplitBlocks, nblk);
-      const int64_t seg0 = ((int64_t)p_rb * nblk + b0) * 16;
-      prefetch_l2(ex.w2.q + seg0 * 32, (uint32_t)(b1 - b0) * 512u);
-      prefetch_l2(ex.w2.absmax + seg0, (uint32_t)(b1 - b0) * 64u);
-    }
-    step(p_ai, p_s, p_rb);
-  };
-  if (threadIdx.x == 0)
-    for (int i = 0; i < kPrefetchItems; ++i) prefetch();
-
-  auto body = [&](const ItemLoads<NBW>& L, int i) {
-    if (threadIdx.x == 0) prefetch();
-    const int e = s_active[c_ai];
-    const int tok0 = s_off[e];
-    const int n = s_off[e + 1] - tok0;
-    if (c_ai != staged_ai || c_s != staged_s) {
-      const int blk0 = c_s * kSplitBlocks + wblk;
-      const int tok = kMulti ? g : 0;
-      const bool valid = tok < n;
-      load_x<NBW>(a.h_sorted + (int64_t)(tok0 + (valid ? tok : 0)) * I, valid, blk0, nblk, t, xr);
-      staged_ai = c_ai;
-      staged_s = c_s;
-    }
-    float acc[4];
-    compute_item<NBW, kMulti>(L, xr, base, acc);
-    const int slot = ((i / B) & 1) * B + i % B;
-    stash<kMulti>(red, slot, warp, g, t, acc);
-    if (warp == 0) s_meta[slot] = SlotMeta{tok0, n, c_rb * 16, c_s};
-    step(c_ai, c_s, c_rb);
-    if (i % B == B - 1 || i == my_items - 1) {
-      __syncthreads();
-      const int i0 = i - i % B, sl0 = ((i0 / B) & 1) * B;
-      const int jobs = (i - i0 + 1) * 16 * red_cols<kMulti>();
-      for (int job = threadIdx.x; job < jobs; job += kThreadsK) {
-        const int bi = job / (16 * red_cols<kMulti>()), rem = job % (16 * red_cols<kMulti>());
-        const int rr = rem & 15, tok = rem >> 4;
-        const SlotMeta m = s_meta[sl0 + bi];
-        if (tok >= m.n) continue;
-        const float ys = reduce_partials<kMulti>(red, sl0 + bi, rr, tok);
-        a.y_part[((int64_t)(m.tok0 + tok) * a.S + m.s) * H + m.row + rr] = ys;
-      }
-    }
-  };
-
-  issue(L0);
-  for (int i = 0; i < my_items; i += 2) {
-    if (i + 1 < my_items) issue(L1);
-    body(L0, i);
-    if (i + 1 >= my_items) break;
-    if (i + 2 < my_items) issue(L0);
-    body(L1, i + 1);
+  if (kMulti) lut_ok = room && build_lut(a.ex.e[0].w1.code, smem);
+  if (!lut_ok) return;
+  const StageSmem sm{reinterpret_cast<float*>(smem), s_off, s_active, s_meta};
+  gate_phase<NBW, kMulti, kFullG>(a, act, sm);
+  if (!same_codebook(a.ex.e[0].w1.code, a.ex.e[0].w2.code)) {
+    __syncthreads();
+    build_lut(a.ex.e[0].w2.code, smem);
   }
+  down_phase<kDownSlice / (64 * kWarpsK), kMulti, kFullD>(a, act, sm);
 }
 
 // y[slot] = fp16(sum over splits of y_part[slot][s]) (single-expert forward).
@@ -552,11 +680,21 @@ __global__ void k_reduce_partials(const float* __restrict__ part, int64_t P, int
   }
 }
 
-__global__ void k_identity_offsets(int32_t* off, int n) {
+// Offsets of one expert holding all n rows; also zeroes the decode launch's
+// completion counters.
+__global__ void k_identity_offsets(int32_t* off, int n, int32_t* zero, int nzero) {
   if (threadIdx.x == 0) {
     off[0] = 0;
     off[1] = n;
   }
+  for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
+}
+
+// Zeroes the decode launch's completion counters (after the predecessor).
+__global__ void k_zero_words(int32_t* p, int n) {
+  pdl_trigger();
+  pdl_wait();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = 0;
 }
 
 template <class K>
@@ -565,58 +703,52 @@ bool smem_attr(K kernel) {
          cudaSuccess;
 }
 
-template <bool kMulti, bool kFull>
-bool attrs_full() {
-  return smem_attr(k_gate_up_mma<1, kMulti, kFull>) && smem_attr(k_gate_up_mma<2, kMulti, kFull>) &&
-         smem_attr(k_gate_up_mma<4, kMulti, kFull>) && smem_attr(k_gate_up_mma<8, kMulti, kFull>) &&
-         smem_attr(k_down_mma<kDownSlice / (64 * kWarpsK), kMulti, kFull>);
+template <int NBW, bool kMulti>
+bool attrs_nbw() {
+  return smem_attr(k_stage_mma<NBW, kMulti, true, true>) &&
+         smem_attr(k_stage_mma<NBW, kMulti, true, false>) &&
+         smem_attr(k_stage_mma<NBW, kMulti, false, true>) &&
+         smem_attr(k_stage_mma<NBW, kMulti, false, false>);
 }
 template <bool kMulti>
 bool attrs() {
-  return attrs_full<kMulti, true>() && attrs_full<kMulti, false>();
+  return attrs_nbw<1, kMulti>() && attrs_nbw<2, kMulti>() && attrs_nbw<4, kMulti>() &&
+         attrs_nbw<8, kMulti>();
 }
 
-// Blocks per K part of the gate_up kernels: ceil(H / 64 / 16) rounded up to
-// a power of two (parts past the row are idle).
+// Blocks per K part of the gate_up phase: ceil(H / 64 / 16) rounded up to a
+// power of two (parts past the row are idle).
 int gate_nbw(int hidden) {
   const int need = static_cast<int>(ceil_div(hidden / 64, kWarpsK));
   return need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : -1;
 }
 
 template <int NBW, bool kMulti>
-cudaError_t launch_gate_nbw(const DecodeArgs& a, cudaStream_t s) {
-  const int grid = sm_count();
-  cudaError_t st;
-  if (a.H / 64 == NBW * kWarpsK)
-    st = launch_pdl(k_gate_up_mma<NBW, kMulti, true>, grid, kThreadsK, kDynSmem, s, a);
-  else
-    st = launch_pdl(k_gate_up_mma<NBW, kMulti, false>, grid, kThreadsK, kDynSmem, s, a);
-  return st;
+cudaError_t launch_stage_nbw(const DecodeArgs& a, cudaStream_t s) {
+  const bool full_g = a.H / 64 == NBW * kWarpsK;
+  const bool full_d = (a.I / 64) % (kDownSlice / 64) == 0;
+  auto k = full_g ? (full_d ? k_stage_mma<NBW, kMulti, true, true> : k_stage_mma<NBW, kMulti, true, false>)
+                  : (full_d ? k_stage_mma<NBW, kMulti, false, true>
+                            : k_stage_mma<NBW, kMulti, false, false>);
+  // One CTA per SM (the CTA takes the whole register file), so the grid is
+  // resident as soon as the predecessor's CTAs leave; the predecessor never
+  // waits on this kernel and the successor starts only after every CTA here
+  // has run its trigger.  A co-resident (cooperative) launch would also hold
+  // when other streams occupy SMs, but it forgoes the programmatic overlap
+  // (about 3 us per layer); the cross-CTA waits are bounded either way.
+  return launch_pdl(k, sm_count(), kThreadsK, kDynSmem, s, a);
 }
 
 template <bool kMulti>
-int launch_gate(const DecodeArgs& a, cudaStream_t s) {
+int launch_stage(const DecodeArgs& a, cudaStream_t s) {
   cudaError_t st;
   switch (gate_nbw(a.H)) {
-    case 1: st = launch_gate_nbw<1, kMulti>(a, s); break;
-    case 2: st = launch_gate_nbw<2, kMulti>(a, s); break;
-    case 4: st = launch_gate_nbw<4, kMulti>(a, s); break;
-    case 8: st = launch_gate_nbw<8, kMulti>(a, s); break;
+    case 1: st = launch_stage_nbw<1, kMulti>(a, s); break;
+    case 2: st = launch_stage_nbw<2, kMulti>(a, s); break;
+    case 4: st = launch_stage_nbw<4, kMulti>(a, s); break;
+    case 8: st = launch_stage_nbw<8, kMulti>(a, s); break;
     default: return MOE_ERR_UNSUPPORTED;
   }
-  if (st != cudaSuccess) return MOE_ERR_CUDA;
-  MOE_CHECK_LAUNCH();
-  return MOE_OK;
-}
-
-template <bool kMulti>
-int launch_down(const DecodeArgs& a, cudaStream_t s) {
-  constexpr int NBW = kDownSlice / (64 * kWarpsK);
-  cudaError_t st;
-  if ((a.I / 64) % (kDownSlice / 64) == 0)
-    st = launch_pdl(k_down_mma<NBW, kMulti, true>, sm_count(), kThreadsK, kDynSmem, s, a);
-  else
-    st = launch_pdl(k_down_mma<NBW, kMulti, false>, sm_count(), kThreadsK, kDynSmem, s, a);
   if (st != cudaSuccess) return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
@@ -633,12 +765,14 @@ bool decode_supported(int hidden, int inter) {
 // Down-projection K splits of 2048 elements (the last may be partial).
 int decode_splits(int inter) { return static_cast<int>(ceil_div(inter, kDownSlice)); }
 int decode_max_tokens() { return kMaxTok; }
+// Completion counters the decode launches need (zeroed before each layer).
+int decode_sync_words(int inter) { return 2 * MOE_MAX_EXPERTS * decode_splits(inter); }
 
 int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t* expert_offsets,
                           const int32_t* pair_token, const uint16_t* x, int hidden, int inter,
-                          uint16_t* h_sorted, float* y_part, int max_tokens_per_expert,
-                          cudaStream_t s) {
-  if (E < 1 || E > MOE_MAX_EXPERTS) return MOE_ERR_INVALID_ARG;
+                          uint16_t* h_sorted, float* y_part, int32_t* sync,
+                          int max_tokens_per_expert, cudaStream_t s) {
+  if (E < 1 || E > MOE_MAX_EXPERTS || !sync) return MOE_ERR_INVALID_ARG;
   if (!decode_supported(hidden, inter)) return MOE_ERR_UNSUPPORTED;
   static bool attr_ok = attrs<false>() && attrs<true>();
   if (!attr_ok) return MOE_ERR_CUDA;
@@ -653,12 +787,23 @@ int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t*
   a.H = hidden;
   a.I = inter;
   a.S = decode_splits(inter);
-  const bool multi = max_tokens_per_expert > 1;
-  int st = launch_gate<false>(a, s);
-  if (st == MOE_OK && multi) st = launch_gate<true>(a, s);
-  if (st == MOE_OK) st = launch_down<false>(a, s);
-  if (st == MOE_OK && multi) st = launch_down<true>(a, s);
+  a.sync = sync;
+  int st = launch_stage<false>(a, s);
+  if (st == MOE_OK && max_tokens_per_expert > 1) {
+    a.sync = sync + MOE_MAX_EXPERTS * a.S;
+    st = launch_stage<true>(a, s);
+  }
   return st;
+}
+
+// Reads and clears the decode error word (a bounded cross-CTA wait timed out).
+int decode_take_error(int* value) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_decode_error, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(g_decode_error, &zero, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
+  *value = v;
+  return MOE_OK;
 }
 
 int launch_reduce_partials(const float* part, int64_t P, int S, int width, uint16_t* y,
@@ -672,8 +817,14 @@ int launch_reduce_partials(const float* part, int64_t P, int S, int width, uint1
   return MOE_OK;
 }
 
-int launch_identity_offsets(int32_t* off, int n, cudaStream_t s) {
-  k_identity_offsets<<<1, 32, 0, s>>>(off, n);
+int launch_zero_words(int32_t* p, int n, cudaStream_t s) {
+  if (launch_pdl(k_zero_words, 1, 256, 0, s, p, n) != cudaSuccess) return MOE_ERR_CUDA;
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
+int launch_identity_offsets(int32_t* off, int n, int32_t* zero, int nzero, cudaStream_t s) {
+  k_identity_offsets<<<1, 256, 0, s>>>(off, n, zero, nzero);
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }

@@ -16,15 +16,17 @@ int decode_splits(int inter);
 int decode_max_tokens();
 int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t* expert_offsets,
                           const int32_t* pair_token, const uint16_t* x, int hidden, int inter,
-                          uint16_t* h_sorted, float* y_part, int max_tokens_per_expert,
-                          cudaStream_t s);
+                          uint16_t* h_sorted, float* y_part, int32_t* sync,
+                          int max_tokens_per_expert, cudaStream_t s);
+int decode_sync_words(int inter);
+int launch_zero_words(int32_t* p, int n, cudaStream_t s);
 int launch_reduce_partials(const float* part, int64_t P, int S, int width, uint16_t* y,
                            cudaStream_t s);
-int launch_identity_offsets(int32_t* off, int n, cudaStream_t s);
+int launch_identity_offsets(int32_t* off, int n, int32_t* zero, int nzero, cudaStream_t s);
 // permute.cu
 int launch_permute(const int64_t* indices, const float* weights, int64_t T, int k, int E,
                    int32_t* expert_offsets, int32_t* pair_token, float* pair_weight,
-                   int32_t* pair_slot, cudaStream_t s);
+                   int32_t* pair_slot, int32_t* zero, int nzero, cudaStream_t s);
 int launch_combine_partials(const float* part, int S, const int32_t* pair_slot,
                             const int64_t* indices, const float* weights, int64_t T, int k,
                             int width, uint16_t* out, cudaStream_t s);
@@ -60,6 +62,7 @@ struct LayerBufs {
   int32_t* pair_slot;
   uint16_t* h_sorted;
   float* y_part;      // decode path
+  int32_t* sync;       // decode path: completion counters
   uint16_t* x_sorted;  // grouped-GEMM path
   uint16_t* y_sorted;  // grouped-GEMM path
 };
@@ -75,9 +78,11 @@ size_t carve_layer(unsigned char* ws, int64_t T, int hidden, int inter, int E, i
   b->h_sorted = c.take<uint16_t>((size_t)P * inter);
   if (use_decode_path(T)) {
     b->y_part = c.take<float>((size_t)P * decode_splits(inter) * hidden);
+    b->sync = c.take<int32_t>(decode_sync_words(inter));
     b->x_sorted = b->y_sorted = nullptr;
   } else {
     b->y_part = nullptr;
+    b->sync = nullptr;
     b->x_sorted = c.take<uint16_t>((size_t)P * hidden);
     b->y_sorted = c.take<uint16_t>((size_t)P * hidden);
   }
@@ -124,12 +129,12 @@ extern "C" int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
   int st = moe_router_topk(h, wg, T, hidden, E, k, nullptr, weights, indices, s);
   if (st != MOE_OK) return st;
   st = launch_permute(indices, weights, T, k, E, b.offsets, b.pair_token, b.pair_weight,
-                      b.pair_slot, s);
+                      b.pair_slot, b.sync, b.sync ? decode_sync_words(inter) : 0, s);
   if (st != MOE_OK) return st;
   const int64_t P = T * k;
   if (use_decode_path(T)) {
     st = launch_decode_experts(experts, E, b.offsets, b.pair_token, h, hidden, inter, b.h_sorted,
-                               b.y_part, static_cast<int>(T), s);
+                               b.y_part, b.sync, static_cast<int>(T), s);
     if (st != MOE_OK) return st;
     return launch_combine_partials(b.y_part, decode_splits(inter), b.pair_slot, indices, weights,
                                    T, k, hidden, out, s);
@@ -148,6 +153,7 @@ struct ExpertBufs {
   int32_t* offsets;
   uint16_t* h;
   float* y_part;
+  int32_t* sync;
 };
 size_t carve_expert(unsigned char* ws, int64_t n, int hidden, int inter, ExpertBufs* b) {
   Carver c{ws};
@@ -155,8 +161,10 @@ size_t carve_expert(unsigned char* ws, int64_t n, int hidden, int inter, ExpertB
   b->h = c.take<uint16_t>((size_t)n * inter);
   if (use_decode_path(n)) {
     b->y_part = c.take<float>((size_t)n * decode_splits(inter) * hidden);
+    b->sync = c.take<int32_t>(decode_sync_words(inter));
   } else {
     b->y_part = nullptr;
+    b->sync = nullptr;
   }
   return c.used;
 }
@@ -183,11 +191,12 @@ extern "C" int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t
   const size_t need = carve_expert(static_cast<unsigned char*>(workspace), n, hidden, inter, &b);
   if (!workspace || workspace_bytes < need) return MOE_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int st = launch_identity_offsets(b.offsets, static_cast<int>(n), s);
+  int st = launch_identity_offsets(b.offsets, static_cast<int>(n), b.sync,
+                                   b.sync ? decode_sync_words(inter) : 0, s);
   if (st != MOE_OK) return st;
   if (use_decode_path(n)) {
     st = launch_decode_experts(expert, 1, b.offsets, nullptr, x, hidden, inter, b.h, b.y_part,
-                               static_cast<int>(n), s);
+                               b.sync, static_cast<int>(n), s);
     if (st != MOE_OK) return st;
     return launch_reduce_partials(b.y_part, n, decode_splits(inter), hidden, y, s);
   }
@@ -202,11 +211,13 @@ namespace {
 struct StageBufs {
   uint16_t* h;
   float* y_part;
+  int32_t* sync;
 };
 size_t carve_stage(unsigned char* ws, int64_t P, int hidden, int inter, StageBufs* b) {
   Carver c{ws};
   b->h = c.take<uint16_t>((size_t)P * inter);
   b->y_part = use_decode_path(P) ? c.take<float>((size_t)P * decode_splits(inter) * hidden) : nullptr;
+  b->sync = use_decode_path(P) ? c.take<int32_t>(decode_sync_words(inter)) : nullptr;
   return c.used;
 }
 }  // namespace
@@ -234,8 +245,10 @@ extern "C" int moe_experts_forward(const moe_nf4_expert_t* experts, int E,
   if (!workspace || workspace_bytes < need) return MOE_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (use_decode_path(P)) {
-    int st = launch_decode_experts(experts, E, expert_offsets, nullptr, x_sorted, hidden, inter,
-                                   b.h, b.y_part, static_cast<int>(P), s);
+    int st = launch_zero_words(b.sync, decode_sync_words(inter), s);
+    if (st != MOE_OK) return st;
+    st = launch_decode_experts(experts, E, expert_offsets, nullptr, x_sorted, hidden, inter,
+                                   b.h, b.y_part, b.sync, static_cast<int>(P), s);
     if (st != MOE_OK) return st;
     return launch_reduce_partials(b.y_part, P, decode_splits(inter), hidden, y_sorted, s);
   }

@@ -18,9 +18,13 @@ constexpr int kPermThreads = 1024;
 __global__ void __launch_bounds__(kPermThreads) k_permute(
     const int64_t* __restrict__ indices, const float* __restrict__ weights, int64_t T, int k,
     int E, int32_t* __restrict__ expert_offsets, int32_t* __restrict__ pair_token,
-    float* __restrict__ pair_weight, int32_t* __restrict__ pair_slot) {
+    float* __restrict__ pair_weight, int32_t* __restrict__ pair_slot, int32_t* __restrict__ zero,
+    int nzero) {
   pdl_trigger();
   pdl_wait();
+  // Completion counters of the expert launch that follows (after the wait:
+  // the previous user of these words has finished).
+  for (int i = threadIdx.x; i < nzero; i += kPermThreads) zero[i] = 0;
   __shared__ int s_count[32];
   __shared__ int s_off[33];
   __shared__ int s_run[32];
@@ -171,9 +175,9 @@ int launch_combine_partials(const float* part, int S, const int32_t* pair_slot,
 
 int launch_permute(const int64_t* indices, const float* weights, int64_t T, int k, int E,
                    int32_t* expert_offsets, int32_t* pair_token, float* pair_weight,
-                   int32_t* pair_slot, cudaStream_t s) {
+                   int32_t* pair_slot, int32_t* zero, int nzero, cudaStream_t s) {
   if (launch_pdl(k_permute, 1, kPermThreads, 0, s, indices, weights, T, k, E, expert_offsets,
-                 pair_token, pair_weight, pair_slot) != cudaSuccess)
+                 pair_token, pair_weight, pair_slot, zero, nzero) != cudaSuccess)
     return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
@@ -198,7 +202,7 @@ extern "C" int moe_permute(const int64_t* indices, const float* weights, int64_t
   if (!indices || !weights || !expert_offsets || !pair_token || !pair_weight || !pair_slot)
     return MOE_ERR_INVALID_ARG;
   return moe::launch_permute(indices, weights, T, k, E, expert_offsets, pair_token, pair_weight,
-                             pair_slot, static_cast<cudaStream_t>(stream));
+                             pair_slot, nullptr, 0, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int moe_gather_rows(const uint16_t* rows_in, const int32_t* index, int64_t n, int width,
