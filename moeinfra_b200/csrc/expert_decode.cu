@@ -88,7 +88,7 @@ __device__ __forceinline__ void cta_range(int total, int* begin, int* end) {
   *end = static_cast<int>(e);
 }
 
-constexpr int kPrefetchItems = 4;  // L2 prefetch distance in items
+constexpr int kPrefetchItems = 2;  // L2 prefetch distance in items
 
 template <int K>
 __device__ __forceinline__ uint32_t perm_addr(uint32_t w, uint32_t base) {
@@ -215,48 +215,78 @@ constexpr int red_floats() {
   return 2 * batch_items<kMulti>() * kWarpsK * 16 * down_tiles<kMulti>() * red_cols<kMulti>();
 }
 
-// Register-resident loads of one item: MMA rows g (qa, sa) and g+8 (qb, sb),
-// blocks kb of this warp's K part.
-template <int NBW>
+// Register-resident loads of one item: MMA rows g (qa) and g+8 (qb), blocks
+// kb of this warp's K part, and the item's absmax.  kS = 0: sa[kb] / sb[kb]
+// are the thread's own (rows g, g+8).  kS = 8 or 16 (cooperative): one load
+// per lane, lane l holding block l / kS, row l % kS of the item's absmax
+// chunk(s); threads fetch theirs with a shuffle (4x fewer load requests).
+template <int NBW, int kS>
 struct ItemLoads {
   uint2 qa[NBW], qb[NBW];
-  float sa[NBW], sb[NBW];
+  float sa[kS ? 1 : NBW], sb[kS ? 1 : NBW];
 };
 
 // qa/qb: byte pointers of the thread's 8-byte segment of block 0 (rows g and
-// g+8); consecutive blocks are 512 bytes apart, their absmax 16 floats apart.
-// Blocks with !valid(kb) read as code 7 (0.0) with absmax 0.
-template <int NBW, bool kFull>
-__device__ __forceinline__ void load_item(ItemLoads<NBW>& L, const uint8_t* qa, const uint8_t* qb,
-                                          const float* sa, const float* sb, int kb_valid) {
+// g+8); consecutive blocks are 512 bytes apart.  Blocks with !valid(kb) read
+// as code 7 (0.0).
+template <int NBW, int kS, bool kFull>
+__device__ __forceinline__ void load_codes(ItemLoads<NBW, kS>& L, const uint8_t* qa,
+                                           const uint8_t* qb, int kb_valid) {
 #pragma unroll
   for (int kb = 0; kb < NBW; ++kb) {
     if (kFull || kb < kb_valid) {
       L.qa[kb] = ldg_stream64(qa + kb * 512);
       L.qb[kb] = ldg_stream64(qb + kb * 512);
-      L.sa[kb] = __ldg(sa + kb * 16);
-      L.sb[kb] = __ldg(sb + kb * 16);
     } else {
       L.qa[kb] = L.qb[kb] = make_uint2(0x77777777u, 0x77777777u);  // NF4 code 7 == 0.0
-      L.sa[kb] = L.sb[kb] = 0.f;
     }
   }
 }
 
+// Per-thread absmax (kS = 0): blocks 16 floats apart; absmax 0 past the row.
+template <int NBW, bool kFull>
+__device__ __forceinline__ void load_abs_own(ItemLoads<NBW, 0>& L, const float* sa, const float* sb,
+                                             int kb_valid) {
+#pragma unroll
+  for (int kb = 0; kb < NBW; ++kb) {
+    const bool ok = kFull || kb < kb_valid;
+    L.sa[kb] = ok ? __ldg(sa + kb * 16) : 0.f;
+    L.sb[kb] = ok ? __ldg(sb + kb * 16) : 0.f;
+  }
+}
+
+// absmax of block kb for the thread's rows g (a) and g+8 (b).
+template <int NBW, int kS>
+__device__ __forceinline__ void item_abs(const ItemLoads<NBW, kS>& L, int kb, int g, float& a,
+                                         float& b) {
+  if (kS == 0) {
+    a = L.sa[kb];
+    b = L.sb[kb];
+  } else if (kS == 8) {  // gate_up: sa = W1 rows, sb = W3 rows of the 8-row item
+    a = __shfl_sync(0xffffffffu, L.sa[0], kb * 8 + g);
+    b = __shfl_sync(0xffffffffu, L.sb[0], kb * 8 + g);
+  } else {  // down: sa = the 16 rows of the tile
+    a = __shfl_sync(0xffffffffu, L.sa[0], kb * 16 + g);
+    b = __shfl_sync(0xffffffffu, L.sa[0], kb * 16 + g + 8);
+  }
+}
+
 // acc[0..1] = MMA row g (columns 2t, 2t+1), acc[2..3] = MMA row g+8.
-template <int NBW, bool kMulti>
-__device__ __forceinline__ void compute_item(const ItemLoads<NBW>& L, const uint32_t (*xr)[8],
-                                             uint32_t base, float* acc) {
+template <int NBW, bool kMulti, int kS>
+__device__ __forceinline__ void compute_item(const ItemLoads<NBW, kS>& L, const uint32_t (*xr)[8],
+                                             uint32_t base, int g, float* acc) {
   acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
 #pragma unroll
   for (int kb = 0; kb < NBW; ++kb) {
+    float sa, sb;
+    item_abs(L, kb, g, sa, sb);
     if (kMulti) {
-      block_mma<true>(L.qa[kb], L.qb[kb], L.sa[kb], L.sb[kb], xr[kb], base, acc);
+      block_mma<true>(L.qa[kb], L.qb[kb], sa, sb, xr[kb], base, acc);
     } else {
       float d[4] = {0.f, 0.f, 0.f, 0.f};
       block_mma<false>(L.qa[kb], L.qb[kb], 0.f, 0.f, xr[kb], base, d);
-      acc[0] = fmaf(L.sa[kb], d[0], acc[0]);
-      acc[2] = fmaf(L.sb[kb], d[2], acc[2]);
+      acc[0] = fmaf(sa, d[0], acc[0]);
+      acc[2] = fmaf(sb, d[2], acc[2]);
     }
   }
 }
@@ -404,21 +434,30 @@ __device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& ac
   const int blk0 = warp * NBW;
   const int kb_valid = nblk - blk0;  // blocks of this warp inside the row
   const int64_t tile_q = (int64_t)nblk * 512, tile_s = (int64_t)nblk * 16;
-  const int thr_q = blk0 * 512 + g * 32 + t * 8, thr_s = blk0 * 16 + g;
+  // Cooperative absmax while the item's chunks fit the warp (NBW <= 4).
+  constexpr int kS = NBW <= 4 ? 8 : 0;
+  const int thr_q = blk0 * 512 + g * 32 + t * 8;
+  const int thr_s = kS ? blk0 * 16 + (lane >> 3) * 16 + (lane & 7) : blk0 * 16 + g;
+  const bool abs_ok = kS == 0 || ((lane >> 3) < NBW && (kFull || (lane >> 3) < kb_valid));
 
   uint32_t xr[NBW][8];
-  ItemLoads<NBW> L0, L1;
+  ItemLoads<NBW, kS> L0, L1;
   Cursor ld{first / per, first % per};  // next item to load
   Cursor cp = ld;                       // next item to compute
   const moe_nf4_expert_t* ld_ex = &a.ex.e[s_active[ld.ai]];
   int staged = -1;
 
-  auto issue = [&](ItemLoads<NBW>& L) {
+  auto issue = [&](ItemLoads<NBW, kS>& L) {
     const int tile = ld.r >> 1, half = ld.r & 1;
     const int64_t qo = tile * tile_q + half * 256 + thr_q;
     const int64_t so = tile * tile_s + half * 8 + thr_s;
-    load_item<NBW, kFull>(L, ld_ex->w1.q + qo, ld_ex->w3.q + qo, ld_ex->w1.absmax + so,
-                          ld_ex->w3.absmax + so, kb_valid);
+    load_codes<NBW, kS, kFull>(L, ld_ex->w1.q + qo, ld_ex->w3.q + qo, kb_valid);
+    if constexpr (kS == 0) {
+      load_abs_own<NBW, kFull>(L, ld_ex->w1.absmax + so, ld_ex->w3.absmax + so, kb_valid);
+    } else {
+      L.sa[0] = abs_ok ? __ldg(ld_ex->w1.absmax + so) : 0.f;
+      L.sb[0] = abs_ok ? __ldg(ld_ex->w3.absmax + so) : 0.f;
+    }
     const int ai = ld.ai;
     ld.next(per);
     if (ld.ai != ai && ld.ai < act.n) ld_ex = &a.ex.e[s_active[ld.ai]];
@@ -441,7 +480,7 @@ __device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& ac
   if (threadIdx.x == 0)
     for (int i = 0; i < kPrefetchItems; ++i) prefetch();
 
-  auto body = [&](const ItemLoads<NBW>& L, int i) {
+  auto body = [&](const ItemLoads<NBW, kS>& L, int i) {
     if (threadIdx.x == 0) prefetch();
     const int e = s_active[cp.ai];
     const int tok0 = s_off[e];
@@ -455,7 +494,7 @@ __device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& ac
       staged = cp.ai;
     }
     float acc[4];
-    compute_item<NBW, kMulti>(L, xr, base, acc);
+    compute_item<NBW, kMulti, kS>(L, xr, base, g, acc);
     const int slot = ((i / B) & 1) * B + i % B;
     stash<kMulti, 16>(red, slot, warp, g, t, acc, 0);
     if (warp == 0) s_meta[slot] = SlotMeta{tok0, n, (cp.r >> 1) * 16 + (cp.r & 1) * 8, 0};
@@ -520,10 +559,13 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
   const uint32_t base = kMulti ? (kLutWin | 128u | ((lane & 15) * 8)) : (kLutWin | (lane * 4));
   const int wblk = warp * NBW;  // this warp's first block within a split
   const int64_t tile_q = (int64_t)nblk * 512, tile_s = (int64_t)nblk * 16;
-  const int thr_q = wblk * 512 + g * 32 + t * 8, thr_s = wblk * 16 + g;
+  // Cooperative absmax: a tile's NBW blocks x 16 rows are contiguous floats.
+  constexpr int kS = NBW <= 2 ? 16 : 0;
+  const int thr_q = wblk * 512 + g * 32 + t * 8;
+  const int thr_s = kS ? wblk * 16 + lane : wblk * 16 + g;
 
   uint32_t xr[NBW][8];
-  ItemLoads<NBW> L0[kT], L1[kT];
+  ItemLoads<NBW, kS> L0[kT], L1[kT];
   // (ai, s, rg) of the next item to load / compute.
   int l_ai = first / per, l_r = first % per;
   int l_s = l_r / groups, l_rg = l_r % groups;
@@ -540,16 +582,21 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
     }
   };
 
-  auto issue = [&](ItemLoads<NBW>* L) {
+  auto issue = [&](ItemLoads<NBW, kS>* L) {
     const int64_t qo = (int64_t)l_rg * kT * tile_q + (int64_t)l_s * kSplitBlocks * 512 + thr_q;
     const int64_t so = (int64_t)l_rg * kT * tile_s + (int64_t)l_s * kSplitBlocks * 16 + thr_s;
     const uint8_t* q = ld_ex->w2.q + qo;
     const float* sc = ld_ex->w2.absmax + so;
     const int kb_valid = nblk - l_s * kSplitBlocks - wblk;
+    const bool abs_ok = kFull || (lane >> 4) < kb_valid;
 #pragma unroll
-    for (int tt = 0; tt < kT; ++tt)
-      load_item<NBW, kFull>(L[tt], q + tt * tile_q, q + tt * tile_q + 256, sc + tt * tile_s,
-                            sc + tt * tile_s + 8, kb_valid);
+    for (int tt = 0; tt < kT; ++tt) {
+      load_codes<NBW, kS, kFull>(L[tt], q + tt * tile_q, q + tt * tile_q + 256, kb_valid);
+      if constexpr (kS == 0)
+        load_abs_own<NBW, kFull>(L[tt], sc + tt * tile_s, sc + tt * tile_s + 8, kb_valid);
+      else
+        L[tt].sa[0] = abs_ok ? __ldg(sc + tt * tile_s) : 0.f;
+    }
     const int ai = l_ai;
     step(l_ai, l_s, l_rg);
     if (l_ai != ai && l_ai < act.n) ld_ex = &a.ex.e[s_active[l_ai]];
@@ -572,7 +619,7 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
   if (threadIdx.x == 0)
     for (int i = 0; i < kPrefetchItems; ++i) prefetch();
 
-  auto body = [&](const ItemLoads<NBW>* L, int i) {
+  auto body = [&](const ItemLoads<NBW, kS>* L, int i) {
     if (threadIdx.x == 0) prefetch();
     const int e = s_active[c_ai];
     const int tok0 = s_off[e];
@@ -592,7 +639,7 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
 #pragma unroll
     for (int tt = 0; tt < kT; ++tt) {
       float acc[4];
-      compute_item<NBW, kMulti>(L[tt], xr, base, acc);
+      compute_item<NBW, kMulti, kS>(L[tt], xr, base, g, acc);
       stash<kMulti, kRows>(red, slot, warp, g, t, acc, tt * 16);
     }
     if (warp == 0) s_meta[slot] = SlotMeta{tok0, n, c_rg * kRows, c_s};
