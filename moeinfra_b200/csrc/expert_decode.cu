@@ -88,7 +88,10 @@ __device__ __forceinline__ void cta_range(int total, int* begin, int* end) {
   *end = static_cast<int>(e);
 }
 
-constexpr int kPrefetchItems = 2;  // L2 prefetch distance in items
+// L2 prefetch distance in items (gate_up items are half tiles and prefetch
+// whole tiles; down items are two tiles).
+constexpr int kPrefetchGate = 2;
+constexpr int kPrefetchDown = 2;
 
 template <int K>
 __device__ __forceinline__ uint32_t perm_addr(uint32_t w, uint32_t base) {
@@ -463,7 +466,7 @@ __device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& ac
     if (ld.ai != ai && ld.ai < act.n) ld_ex = &a.ex.e[s_active[ld.ai]];
   };
   // One thread pulls the whole 16-row tile (W1, W3, both absmax) of an item
-  // kPrefetchItems ahead into L2 when that item starts a tile.
+  // kPrefetchGate ahead into L2 when that item starts a tile.
   Cursor pf = cp;
   auto prefetch = [&]() {
     if (pf.ai < act.n && (pf.r & 1) == 0) {
@@ -478,7 +481,7 @@ __device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& ac
     pf.next(per);
   };
   if (threadIdx.x == 0)
-    for (int i = 0; i < kPrefetchItems; ++i) prefetch();
+    for (int i = 0; i < kPrefetchGate; ++i) prefetch();
 
   auto body = [&](const ItemLoads<NBW, kS>& L, int i) {
     if (threadIdx.x == 0) prefetch();
@@ -617,7 +620,7 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
     step(p_ai, p_s, p_rg);
   };
   if (threadIdx.x == 0)
-    for (int i = 0; i < kPrefetchItems; ++i) prefetch();
+    for (int i = 0; i < kPrefetchDown; ++i) prefetch();
 
   auto body = [&](const ItemLoads<NBW, kS>* L, int i) {
     if (threadIdx.x == 0) prefetch();
