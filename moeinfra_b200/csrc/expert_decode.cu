@@ -74,9 +74,14 @@ __device__ __forceinline__ float2 lds64f(uint32_t addr) {
 __device__ __forceinline__ uint2 ldg_stream64(const uint8_t* p) {
   return __ldcs(reinterpret_cast<const uint2*>(p));
 }
-// Hint: pull [p, p + bytes) into L2 (bytes a multiple of 16, p 16-byte aligned).
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+// Hint: pull [p, p + bytes) into L2 (bytes a multiple of 16, p 16-byte
+// aligned) when pred is set; a predicated instruction, not a branch.
+__device__ __forceinline__ void prefetch_l2_if(bool pred, const void* p, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t"
+      "@q cp.async.bulk.prefetch.L2.global [%0], %1;\n\t}" ::"l"(p),
+      "r"(bytes), "r"((uint32_t)pred)
+      : "memory");
 }
 
 // Contiguous item range [begin, end) of this CTA (neighbouring items share
@@ -436,7 +441,7 @@ __device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& ac
   const uint32_t base = kMulti ? (kLutWin | 128u | ((lane & 15) * 8)) : (kLutWin | (lane * 4));
   const int blk0 = warp * NBW;
   const int kb_valid = nblk - blk0;  // blocks of this warp inside the row
-  const int64_t tile_q = (int64_t)nblk * 512, tile_s = (int64_t)nblk * 16;
+  const uint32_t tile_q = nblk * 512u, tile_s = nblk * 16u;
   // Cooperative absmax while the item's chunks fit the warp (NBW <= 4).
   constexpr int kS = NBW <= 4 ? 8 : 0;
   const int thr_q = blk0 * 512 + g * 32 + t * 8;
@@ -445,50 +450,69 @@ __device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& ac
 
   uint32_t xr[NBW][8];
   ItemLoads<NBW, kS> L0, L1;
-  Cursor ld{first / per, first % per};  // next item to load
-  Cursor cp = ld;                       // next item to compute
-  const moe_nf4_expert_t* ld_ex = &a.ex.e[s_active[ld.ai]];
-  int staged = -1;
+  // Load cursor: the load expert's per-lane bases and the next item's offsets
+  // in it, advanced without multiplies (half 0 -> 1: +256 / +8; next tile).
+  Cursor ld{first / per, first % per};
+  const uint8_t *q1, *q3;
+  const float *s1, *s3;
+  auto ld_expert = [&](int ai) {
+    const moe_nf4_expert_t& ex = a.ex.e[s_active[ai]];
+    q1 = ex.w1.q + thr_q;
+    q3 = ex.w3.q + thr_q;
+    s1 = ex.w1.absmax + thr_s;
+    s3 = ex.w3.absmax + thr_s;
+  };
+  ld_expert(ld.ai);
+  uint32_t qo = (ld.r >> 1) * tile_q + (ld.r & 1) * 256u;
+  uint32_t so = (ld.r >> 1) * tile_s + (ld.r & 1) * 8u;
 
   auto issue = [&](ItemLoads<NBW, kS>& L) {
-    const int tile = ld.r >> 1, half = ld.r & 1;
-    const int64_t qo = tile * tile_q + half * 256 + thr_q;
-    const int64_t so = tile * tile_s + half * 8 + thr_s;
-    load_codes<NBW, kS, kFull>(L, ld_ex->w1.q + qo, ld_ex->w3.q + qo, kb_valid);
+    load_codes<NBW, kS, kFull>(L, q1 + qo, q3 + qo, kb_valid);
     if constexpr (kS == 0) {
-      load_abs_own<NBW, kFull>(L, ld_ex->w1.absmax + so, ld_ex->w3.absmax + so, kb_valid);
+      load_abs_own<NBW, kFull>(L, s1 + so, s3 + so, kb_valid);
     } else {
-      L.sa[0] = abs_ok ? __ldg(ld_ex->w1.absmax + so) : 0.f;
-      L.sb[0] = abs_ok ? __ldg(ld_ex->w3.absmax + so) : 0.f;
+      L.sa[0] = abs_ok ? __ldg(s1 + so) : 0.f;
+      L.sb[0] = abs_ok ? __ldg(s3 + so) : 0.f;
     }
-    const int ai = ld.ai;
-    ld.next(per);
-    if (ld.ai != ai && ld.ai < act.n) ld_ex = &a.ex.e[s_active[ld.ai]];
+    if (++ld.r == per) {
+      ld.r = 0;
+      qo = so = 0;
+      if (++ld.ai < act.n) ld_expert(ld.ai);
+    } else {
+      const bool odd = ld.r & 1;
+      qo += odd ? 256u : tile_q - 256u;
+      so += odd ? 8u : tile_s - 8u;
+    }
   };
-  // One thread pulls the whole 16-row tile (W1, W3, both absmax) of an item
-  // kPrefetchGate ahead into L2 when that item starts a tile.
-  Cursor pf = cp;
+  // Warp 0 walks the prefetch cursor; its lane 0 pulls the whole 16-row tile
+  // (W1, W3, both absmax) of an item kPrefetchGate ahead into L2 when that
+  // item starts a tile.
+  Cursor pf = ld;
   auto prefetch = [&]() {
     if (pf.ai < act.n && (pf.r & 1) == 0) {
       const moe_nf4_expert_t& ex = a.ex.e[s_active[pf.ai]];
-      const int64_t tile = pf.r >> 1;
+      const uint32_t tile = pf.r >> 1;
       const uint32_t qbytes = 16u * (H / 2), abytes = 16u * (H / 64) * 4u;
-      prefetch_l2(ex.w1.q + tile * qbytes, qbytes);
-      prefetch_l2(ex.w3.q + tile * qbytes, qbytes);
-      prefetch_l2(ex.w1.absmax + tile * (abytes / 4), abytes);
-      prefetch_l2(ex.w3.absmax + tile * (abytes / 4), abytes);
+      const bool p = lane == 0;
+      prefetch_l2_if(p, ex.w1.q + (size_t)tile * qbytes, qbytes);
+      prefetch_l2_if(p, ex.w3.q + (size_t)tile * qbytes, qbytes);
+      prefetch_l2_if(p, ex.w1.absmax + (size_t)tile * (abytes / 4), abytes);
+      prefetch_l2_if(p, ex.w3.absmax + (size_t)tile * (abytes / 4), abytes);
     }
     pf.next(per);
   };
-  if (threadIdx.x == 0)
+  if (warp == 0)
     for (int i = 0; i < kPrefetchGate; ++i) prefetch();
 
+  // Compute cursor and its expert's token range.
+  Cursor cp = ld;
+  int staged = -1, tok0 = 0, n = 0;
   auto body = [&](const ItemLoads<NBW, kS>& L, int i) {
-    if (threadIdx.x == 0) prefetch();
-    const int e = s_active[cp.ai];
-    const int tok0 = s_off[e];
-    const int n = s_off[e + 1] - tok0;
+    if (warp == 0) prefetch();
     if (cp.ai != staged) {
+      const int e = s_active[cp.ai];
+      tok0 = s_off[e];
+      n = s_off[e + 1] - tok0;
       const int tok = kMulti ? g : 0;
       const bool valid = tok < n;
       const int64_t xrow =
@@ -509,12 +533,12 @@ __device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& ac
       const int jobs = (i - i0 + 1) * 8 * red_cols<kMulti>();
       for (int job = threadIdx.x; job < jobs; job += kThreadsK) {
         const int bi = job / (8 * red_cols<kMulti>()), rem = job % (8 * red_cols<kMulti>());
-        const int rr = rem & 7, tok = rem >> 3;
+        const int rr = rem & 7, tk = rem >> 3;
         const SlotMeta m = s_meta[sl0 + bi];
-        if (tok >= m.n) continue;
-        const float gs = reduce_partials<kMulti, 16>(red, sl0 + bi, rr, tok);
-        const float us = reduce_partials<kMulti, 16>(red, sl0 + bi, rr + 8, tok);
-        a.h_sorted[(int64_t)(m.tok0 + tok) * I + m.row + rr] = swiglu_f16(f2h(gs), f2h(us));
+        if (tk >= m.n) continue;
+        const float gs = reduce_partials<kMulti, 16>(red, sl0 + bi, rr, tk);
+        const float us = reduce_partials<kMulti, 16>(red, sl0 + bi, rr + 8, tk);
+        a.h_sorted[(int64_t)(m.tok0 + tk) * I + m.row + rr] = swiglu_f16(f2h(gs), f2h(us));
       }
     }
   };
@@ -561,7 +585,7 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
   SlotMeta* s_meta = sm.s_meta;
   const uint32_t base = kMulti ? (kLutWin | 128u | ((lane & 15) * 8)) : (kLutWin | (lane * 4));
   const int wblk = warp * NBW;  // this warp's first block within a split
-  const int64_t tile_q = (int64_t)nblk * 512, tile_s = (int64_t)nblk * 16;
+  const uint32_t tile_q = nblk * 512u, tile_s = nblk * 16u;
   // Cooperative absmax: a tile's NBW blocks x 16 rows are contiguous floats.
   constexpr int kS = NBW <= 2 ? 16 : 0;
   const int thr_q = wblk * 512 + g * 32 + t * 8;
@@ -569,65 +593,82 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
 
   uint32_t xr[NBW][8];
   ItemLoads<NBW, kS> L0[kT], L1[kT];
-  // (ai, s, rg) of the next item to load / compute.
+  // Load cursor (ai, s, rg), the load expert's per-lane bases and the item's
+  // offsets in them (next group: + kT tiles; next split: its first block).
   int l_ai = first / per, l_r = first % per;
   int l_s = l_r / groups, l_rg = l_r % groups;
-  int c_ai = l_ai, c_s = l_s, c_rg = l_rg;
-  const moe_nf4_expert_t* ld_ex = &a.ex.e[s_active[l_ai]];
-  int staged_ai = -1, staged_s = -1;
-  auto step = [&](int& ai, int& s, int& rg) {
-    if (++rg == groups) {
-      rg = 0;
-      if (++s == a.S) {
-        s = 0;
-        ++ai;
-      }
-    }
+  const uint8_t* qb;
+  const float* sb;
+  auto ld_expert = [&](int ai) {
+    const moe_nf4_expert_t& ex = a.ex.e[s_active[ai]];
+    qb = ex.w2.q + thr_q;
+    sb = ex.w2.absmax + thr_s;
   };
+  ld_expert(l_ai);
+  uint32_t qo = l_rg * kT * tile_q + l_s * (kSplitBlocks * 512u);
+  uint32_t so = l_rg * kT * tile_s + l_s * (kSplitBlocks * 16u);
+  int kb_valid = nblk - l_s * kSplitBlocks - wblk;
+  const int c_first_ai = l_ai, c_first_s = l_s, c_first_rg = l_rg;
 
   auto issue = [&](ItemLoads<NBW, kS>* L) {
-    const int64_t qo = (int64_t)l_rg * kT * tile_q + (int64_t)l_s * kSplitBlocks * 512 + thr_q;
-    const int64_t so = (int64_t)l_rg * kT * tile_s + (int64_t)l_s * kSplitBlocks * 16 + thr_s;
-    const uint8_t* q = ld_ex->w2.q + qo;
-    const float* sc = ld_ex->w2.absmax + so;
-    const int kb_valid = nblk - l_s * kSplitBlocks - wblk;
     const bool abs_ok = kFull || (lane >> 4) < kb_valid;
 #pragma unroll
     for (int tt = 0; tt < kT; ++tt) {
-      load_codes<NBW, kS, kFull>(L[tt], q + tt * tile_q, q + tt * tile_q + 256, kb_valid);
+      load_codes<NBW, kS, kFull>(L[tt], qb + qo + tt * tile_q, qb + qo + tt * tile_q + 256, kb_valid);
       if constexpr (kS == 0)
-        load_abs_own<NBW, kFull>(L[tt], sc + tt * tile_s, sc + tt * tile_s + 8, kb_valid);
+        load_abs_own<NBW, kFull>(L[tt], sb + so + tt * tile_s, sb + so + tt * tile_s + 8, kb_valid);
       else
-        L[tt].sa[0] = abs_ok ? __ldg(sc + tt * tile_s) : 0.f;
+        L[tt].sa[0] = abs_ok ? __ldg(sb + so + tt * tile_s) : 0.f;
     }
-    const int ai = l_ai;
-    step(l_ai, l_s, l_rg);
-    if (l_ai != ai && l_ai < act.n) ld_ex = &a.ex.e[s_active[l_ai]];
+    if (++l_rg < groups) {
+      qo += kT * tile_q;
+      so += kT * tile_s;
+    } else {
+      l_rg = 0;
+      if (++l_s == a.S) {
+        l_s = 0;
+        if (++l_ai < act.n) ld_expert(l_ai);
+      }
+      qo = l_s * (kSplitBlocks * 512u);
+      so = l_s * (kSplitBlocks * 16u);
+      kb_valid = nblk - l_s * kSplitBlocks - wblk;
+    }
   };
-  // One thread pulls an upcoming item's blocks (contiguous in tile16) into L2.
-  int p_ai = c_ai, p_s = c_s, p_rg = c_rg;
+  // Warp 0 walks the prefetch cursor; its lane 0 pulls an upcoming item's
+  // blocks (contiguous in tile16) into L2.
+  int p_ai = c_first_ai, p_s = c_first_s, p_rg = c_first_rg;
   auto prefetch = [&]() {
     if (p_ai < act.n) {
       const moe_nf4_expert_t& ex = a.ex.e[s_active[p_ai]];
       const int b0 = p_s * kSplitBlocks, b1 = min(b0 + kSplitBlocks, nblk);
+      const bool p = lane == 0;
 #pragma unroll
       for (int tt = 0; tt < kT; ++tt) {
         const int64_t seg0 = ((int64_t)(p_rg * kT + tt) * nblk + b0) * 16;
-        prefetch_l2(ex.w2.q + seg0 * 32, (uint32_t)(b1 - b0) * 512u);
-        prefetch_l2(ex.w2.absmax + seg0, (uint32_t)(b1 - b0) * 64u);
+        prefetch_l2_if(p, ex.w2.q + seg0 * 32, (uint32_t)(b1 - b0) * 512u);
+        prefetch_l2_if(p, ex.w2.absmax + seg0, (uint32_t)(b1 - b0) * 64u);
       }
     }
-    step(p_ai, p_s, p_rg);
+    if (++p_rg == groups) {
+      p_rg = 0;
+      if (++p_s == a.S) {
+        p_s = 0;
+        ++p_ai;
+      }
+    }
   };
-  if (threadIdx.x == 0)
+  if (warp == 0)
     for (int i = 0; i < kPrefetchDown; ++i) prefetch();
 
+  // Compute cursor, its expert's token range and the staged (expert, split).
+  int c_ai = c_first_ai, c_s = c_first_s, c_rg = c_first_rg;
+  int staged_ai = -1, staged_s = -1, tok0 = 0, n = 0;
   auto body = [&](const ItemLoads<NBW, kS>* L, int i) {
-    if (threadIdx.x == 0) prefetch();
-    const int e = s_active[c_ai];
-    const int tok0 = s_off[e];
-    const int n = s_off[e + 1] - tok0;
+    if (warp == 0) prefetch();
     if (c_ai != staged_ai || c_s != staged_s) {
+      const int e = s_active[c_ai];
+      tok0 = s_off[e];
+      n = s_off[e + 1] - tok0;
       // h rows of this split come from other CTAs' gate_up items.
       wait_count(a.sync + c_ai * a.S + c_s, split_items(I, c_s));
       const int blk0 = c_s * kSplitBlocks + wblk;
@@ -646,18 +687,24 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
       stash<kMulti, kRows>(red, slot, warp, g, t, acc, tt * 16);
     }
     if (warp == 0) s_meta[slot] = SlotMeta{tok0, n, c_rg * kRows, c_s};
-    step(c_ai, c_s, c_rg);
+    if (++c_rg == groups) {
+      c_rg = 0;
+      if (++c_s == a.S) {
+        c_s = 0;
+        ++c_ai;
+      }
+    }
     if (i % B == B - 1 || i == my_items - 1) {
       __syncthreads();
       const int i0 = i - i % B, sl0 = ((i0 / B) & 1) * B;
       const int jobs = (i - i0 + 1) * kRows * C;
       for (int job = threadIdx.x; job < jobs; job += kThreadsK) {
         const int bi = job / (kRows * C), rem = job % (kRows * C);
-        const int rr = rem % kRows, tok = rem / kRows;
+        const int rr = rem % kRows, tk = rem / kRows;
         const SlotMeta m = s_meta[sl0 + bi];
-        if (tok >= m.n) continue;
-        const float ys = reduce_partials<kMulti, kRows>(red, sl0 + bi, rr, tok);
-        a.y_part[((int64_t)(m.tok0 + tok) * a.S + m.s) * H + m.row + rr] = ys;
+        if (tk >= m.n) continue;
+        const float ys = reduce_partials<kMulti, kRows>(red, sl0 + bi, rr, tk);
+        a.y_part[((int64_t)(m.tok0 + tk) * a.S + m.s) * H + m.row + rr] = ys;
       }
     }
   };
@@ -809,7 +856,8 @@ int launch_stage(const DecodeArgs& a, cudaStream_t s) {
 // Shapes the decode kernels accept: H and I multiples of 64 (one absmax block)
 // with H up to 8192.
 bool decode_supported(int hidden, int inter) {
-  return hidden > 0 && inter > 0 && hidden % 64 == 0 && inter % 64 == 0 && gate_nbw(hidden) > 0;
+  return hidden > 0 && inter > 0 && hidden % 64 == 0 && inter % 64 == 0 && gate_nbw(hidden) > 0 &&
+         (int64_t)hidden * inter / 2 < ((int64_t)1 << 31);  // 32-bit offsets within a matrix
 }
 
 // Down-projection K splits of 2048 elements (the last may be partial).
