@@ -32,6 +32,7 @@
 //   down   : item = (16 rows, K split s of 2048 elements); split partials go
 //            to y_part[slot][S][H] and the combine kernel sums them in order.
 #include "common.cuh"
+#include "router_device.cuh"
 
 namespace moe {
 namespace {
@@ -53,6 +54,14 @@ struct DecodeArgs {
   float* y_part;                  // fp32 [P][S][H]
   int* sync;                      // [MOE_MAX_EXPERTS][S] gate_up completion counters, zeroed
   int H, I, S;
+  // Fused 1-token layer (route_wg != null): every CTA routes the token x[0]
+  // itself; the last CTA to finish a row group writes its weighted combine.
+  const uint16_t* route_wg;  // fp16 gate weights [E][H]
+  int route_k;
+  float* out_weights;        // [k] routing weights (written by CTA 0)
+  int64_t* out_indices;      // [k] routed experts (written by CTA 0)
+  uint16_t* out;             // [H] fp16 layer output
+  int* rg_count;             // [H / 16] row-group completion counters, zeroed
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -417,6 +426,7 @@ struct StageSmem {
   const int* s_off;
   const int* s_active;
   SlotMeta* s_meta;
+  const int32_t* pair_token;  // token row of each sorted pair (null: identity)
 };
 
 // gate_up phase.  NBW = 64-element blocks per warp (16 warps split H).  Item =
@@ -516,7 +526,7 @@ __device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& ac
       const int tok = kMulti ? g : 0;
       const bool valid = tok < n;
       const int64_t xrow =
-          valid ? (a.pair_token ? a.pair_token[tok0 + tok] : (int64_t)(tok0 + tok)) : 0;
+          valid ? (sm.pair_token ? sm.pair_token[tok0 + tok] : (int64_t)(tok0 + tok)) : 0;
       load_x<NBW, false>(a.x + xrow * H, valid, blk0, nblk, t, xr);
       staged = cp.ai;
     }
@@ -719,6 +729,143 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused 1-token layer: routing in every CTA, combine by row-group last arrivers.
+
+// Routing of the layer's single token, identical in every CTA.
+struct RouteSmem {
+  route::FF part[kWarpsK];
+  float w[8];          // routing weights in top-k output order
+  int64_t idx[8];      // routed experts in top-k output order
+  float w_slot[8];     // weight of the pair at sorted position p (ascending expert id)
+  int32_t zero_tok[8];  // every pair reads token row 0
+};
+
+// Logits by the exact double-float gate dot products (warp w: expert w % E,
+// range w / E of the row), softmax and top-k as the router kernels; then the
+// counting sort of the k pairs by expert (offsets, active experts).
+__device__ __forceinline__ Active route_token(const DecodeArgs& a, int* s_off, int* s_active,
+                                              RouteSmem& rs) {
+  __shared__ int s_n;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int E = a.E, k = a.route_k, H = a.H;
+  const int nvec = H >> 3;
+  const int groups = kWarpsK / E;  // >= 1 (E <= 16)
+  if (warp < groups * E) {
+    const int e = warp % E, r = warp / E;
+    const int v0 = nvec * r / groups, v1 = nvec * (r + 1) / groups;
+    const uint4* hrow = reinterpret_cast<const uint4*>(a.x);
+    const uint4* wrow = reinterpret_cast<const uint4*>(a.route_wg) + (int64_t)e * nvec;
+    route::FF acc{0.f, 0.f};
+    constexpr int U = 4;
+    for (int vb = v0 + lane; vb < v1; vb += 32 * U) {
+      uint4 hv[U], wv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int v = vb + u * 32;
+        hv[u] = v < v1 ? hrow[v] : make_uint4(0, 0, 0, 0);
+        wv[u] = v < v1 ? __ldg(wrow + v) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const __half2* hh = reinterpret_cast<const __half2*>(&hv[u]);
+        const __half2* ww = reinterpret_cast<const __half2*>(&wv[u]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 x = __half22float2(hh[q]), y = __half22float2(ww[q]);
+          route::ff_add(acc, __fmul_rn(x.x, y.x));
+          route::ff_add(acc, __fmul_rn(x.y, y.y));
+        }
+      }
+    }
+    const route::FF tot = route::warp_sum_ff(acc);
+    if (lane == 0) rs.part[warp] = tot;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int W = 1;
+    while (W < E) W <<= 1;
+    double mine = 0.0;
+    if (lane < E) {
+      route::FF tot = rs.part[lane];
+      for (int r = 1; r < groups; ++r) route::ff_merge(tot, rs.part[r * E + lane]);
+      mine = route::ff_value(tot);
+    }
+    route::finish_token(mine, lane, E, W, k, 0, nullptr, rs.w, rs.idx);
+    __syncwarp();
+    // Stable counting sort of the k pairs (distinct experts) by expert id.
+    int cnt = 0;
+    for (int j = 0; j < k; ++j) cnt += (lane < E && rs.idx[j] == lane) ? 1 : 0;
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 0) s_off[0] = 0;
+    if (lane < E) s_off[lane + 1] = incl;
+    const unsigned act = __ballot_sync(0xffffffffu, lane < E && cnt == 1);
+    if (lane < E && cnt == 1) s_active[__popc(act & ((1u << lane) - 1u))] = lane;
+    if (lane == 0) s_n = __popc(act);
+    if (lane < 8) rs.zero_tok[lane] = 0;
+    __syncwarp();
+    if (lane < k) {
+      rs.w_slot[s_off[rs.idx[lane]]] = rs.w[lane];
+      if (blockIdx.x == 0) {
+        a.out_weights[lane] = rs.w[lane];
+        a.out_indices[lane] = rs.idx[lane];
+      }
+    }
+  }
+  __syncthreads();
+  return Active{s_n, s_n > 0 ? s_active[0] : 0};
+}
+
+// After the down phase: publish this CTA's down items per row group; a CTA
+// that completes a row group (every active expert and split) writes the
+// layer output of those rows: y_e = fp16(sum over splits, in order), then
+// out = fp16(out + y_e * w_e) over the token's experts in ascending id.
+template <bool kMulti>
+__device__ __forceinline__ void combine_rows(const DecodeArgs& a, const Active& act,
+                                             const RouteSmem& rs) {
+  constexpr int kRows = 16 * down_tiles<kMulti>();
+  constexpr int kChunk = 64;
+  __shared__ int s_won[kChunk];
+  __shared__ int s_nwon;
+  const int groups = a.H / kRows, per = a.S * groups;
+  int first, last;
+  cta_range(act.n * per, &first, &last);
+  const int target = act.n * a.S;
+  const int k = a.route_k, S = a.S, H = a.H;
+  for (int c0 = first; c0 < last; c0 += kChunk) {
+    const int c1 = min(last, c0 + kChunk);
+    __syncthreads();  // this CTA's y_part stores (and the previous chunk's reads) are done
+    if (threadIdx.x == 0) {
+      fence_release_gpu();
+      int nw = 0;
+      for (int i = c0; i < c1; ++i) {
+        const int rg = (i % per) % groups;
+        if (atomicAdd(a.rg_count + rg, 1) == target - 1) s_won[nw++] = rg;
+      }
+      fence_release_gpu();  // acquire side: the other CTAs' partials of won groups
+      s_nwon = nw;
+    }
+    __syncthreads();
+    const int nw = s_nwon;
+    for (int job = threadIdx.x; job < nw * kRows; job += blockDim.x) {
+      const int c = s_won[job / kRows] * kRows + job % kRows;
+      float acc = 0.f;
+      for (int p = 0; p < k; ++p) {
+        const float* src = a.y_part + (int64_t)p * S * H + c;
+        float ys = __ldcg(src);
+        for (int sp = 1; sp < S; ++sp) ys = __fadd_rn(ys, __ldcg(src + (int64_t)sp * H));
+        acc = h2f(f2h(__fadd_rn(acc, __fmul_rn(h2f(f2h(ys)), rs.w_slot[p]))));
+      }
+      a.out[c] = f2h(acc);
+    }
+  }
+}
+
 __device__ __forceinline__ bool same_codebook(const float* a, const float* b) {
   if (a == b) return true;
   bool same = true;
@@ -743,21 +890,26 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_stage_mma(const __grid_constan
   // The 1-token launch, first in a layer, builds it before waiting for the
   // kernel that produced its inputs; the 2..8-token launch follows a
   // full-grid kernel (nothing to overlap) and first checks it has work.
+  __shared__ RouteSmem s_route;
   pdl_trigger();
   const bool room = smem_u32(smem) + red_floats<kMulti>() * 4 <= kLutWin;
   bool lut_ok = !kMulti && room && build_lut(a.ex.e[0].w1.code, smem);
   pdl_wait();
-  const Active act = load_active<kMulti>(a, s_off, s_active);
+  const bool routed = !kMulti && a.route_wg != nullptr;
+  const Active act =
+      routed ? route_token(a, s_off, s_active, s_route) : load_active<kMulti>(a, s_off, s_active);
   if (act.n == 0) return;
   if (kMulti) lut_ok = room && build_lut(a.ex.e[0].w1.code, smem);
   if (!lut_ok) return;
-  const StageSmem sm{reinterpret_cast<float*>(smem), s_off, s_active, s_meta};
+  const StageSmem sm{reinterpret_cast<float*>(smem), s_off, s_active, s_meta,
+                     routed ? s_route.zero_tok : a.pair_token};
   gate_phase<NBW, kMulti, kFullG>(a, act, sm);
   if (!same_codebook(a.ex.e[0].w1.code, a.ex.e[0].w2.code)) {
     __syncthreads();
     build_lut(a.ex.e[0].w2.code, smem);
   }
   down_phase<kDownSlice / (64 * kWarpsK), kMulti, kFullD>(a, act, sm);
+  if (routed) combine_rows<kMulti>(a, act, s_route);
 }
 
 // y[slot] = fp16(sum over splits of y_part[slot][s]) (single-expert forward).
@@ -892,6 +1044,37 @@ int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t*
     st = launch_stage<true>(a, s);
   }
   return st;
+}
+
+// One launch for a 1-token layer: routing, gate_up, down and the weighted
+// combine (the permute of one token is a sort of its k distinct experts).
+int launch_decode_layer1(const moe_nf4_expert_t* experts, int E, int k, const uint16_t* h,
+                         const uint16_t* wg, int hidden, int inter, uint16_t* h_sorted,
+                         float* y_part, int32_t* sync, int32_t* rg_count, uint16_t* out,
+                         int64_t* indices, float* weights, cudaStream_t s) {
+  if (E < 1 || E > MOE_MAX_EXPERTS || E > kWarpsK || k < 1 || k > 8 || k > E || !sync ||
+      !rg_count)
+    return MOE_ERR_INVALID_ARG;
+  if (!decode_supported(hidden, inter)) return MOE_ERR_UNSUPPORTED;
+  static bool attr_ok = attrs<false>() && attrs<true>();
+  if (!attr_ok) return MOE_ERR_CUDA;
+  DecodeArgs a{};
+  for (int e = 0; e < E; ++e) a.ex.e[e] = experts[e];
+  a.E = E;
+  a.x = h;
+  a.h_sorted = h_sorted;
+  a.y_part = y_part;
+  a.H = hidden;
+  a.I = inter;
+  a.S = decode_splits(inter);
+  a.sync = sync;
+  a.route_wg = wg;
+  a.route_k = k;
+  a.out_weights = weights;
+  a.out_indices = indices;
+  a.out = out;
+  a.rg_count = rg_count;
+  return launch_stage<false>(a, s);
 }
 
 // Reads and clears the decode error word (a bounded cross-CTA wait timed out).

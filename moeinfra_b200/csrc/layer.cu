@@ -20,6 +20,10 @@ int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t*
                           int max_tokens_per_expert, cudaStream_t s);
 int decode_sync_words(int inter);
 int launch_zero_words(int32_t* p, int n, cudaStream_t s);
+int launch_decode_layer1(const moe_nf4_expert_t* experts, int E, int k, const uint16_t* h,
+                         const uint16_t* wg, int hidden, int inter, uint16_t* h_sorted,
+                         float* y_part, int32_t* sync, int32_t* rg_count, uint16_t* out,
+                         int64_t* indices, float* weights, cudaStream_t s);
 int launch_reduce_partials(const float* part, int64_t P, int S, int width, uint16_t* y,
                            cudaStream_t s);
 int launch_identity_offsets(int32_t* off, int n, int32_t* zero, int nzero, cudaStream_t s);
@@ -62,7 +66,7 @@ struct LayerBufs {
   int32_t* pair_slot;
   uint16_t* h_sorted;
   float* y_part;      // decode path
-  int32_t* sync;       // decode path: completion counters
+  int32_t* sync;       // decode path: completion counters (gate_up splits, then row groups)
   uint16_t* x_sorted;  // grouped-GEMM path
   uint16_t* y_sorted;  // grouped-GEMM path
 };
@@ -78,7 +82,7 @@ size_t carve_layer(unsigned char* ws, int64_t T, int hidden, int inter, int E, i
   b->h_sorted = c.take<uint16_t>((size_t)P * inter);
   if (use_decode_path(T)) {
     b->y_part = c.take<float>((size_t)P * decode_splits(inter) * hidden);
-    b->sync = c.take<int32_t>(decode_sync_words(inter));
+    b->sync = c.take<int32_t>(decode_sync_words(inter) + hidden / 16);
     b->x_sorted = b->y_sorted = nullptr;
   } else {
     b->y_part = nullptr;
@@ -126,6 +130,14 @@ extern "C" int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
   const size_t need = carve_layer(static_cast<unsigned char*>(workspace), T, hidden, inter, E, k, &b);
   if (!workspace || workspace_bytes < need) return MOE_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T == 1 && E <= MOE_MAX_EXPERTS) {
+    // One token: counters zeroed, then a single launch (route, experts, combine).
+    const int words = decode_sync_words(inter);
+    int st = launch_zero_words(b.sync, words + hidden / 16, s);
+    if (st != MOE_OK) return st;
+    return launch_decode_layer1(experts, E, k, h, wg, hidden, inter, b.h_sorted, b.y_part, b.sync,
+                                b.sync + words, out, indices, weights, s);
+  }
   int st = moe_router_topk(h, wg, T, hidden, E, k, nullptr, weights, indices, s);
   if (st != MOE_OK) return st;
   st = launch_permute(indices, weights, T, k, E, b.offsets, b.pair_token, b.pair_weight,
