@@ -153,16 +153,19 @@ __device__ __forceinline__ bool build_lut(const float* __restrict__ code, const 
   if (threadIdx.x < 16) s_code[threadIdx.x] = code[threadIdx.x];
   __syncthreads();
   if (ok) {
-    for (int i = threadIdx.x; i < 256 * 64; i += blockDim.x) {
-      const int v = i >> 6, j = i & 63;
-      uint32_t val;
-      if (j < 32) {
+    // Entry v: 32 words of the fp16 pair, then 16 fp32 pairs; 16-byte stores.
+    for (int i = threadIdx.x; i < 256 * 16; i += blockDim.x) {
+      const int v = i >> 4, q = i & 15;
+      uint32_t w0, w1;
+      if (q < 8) {
         __half2 h = __floats2half2_rn(s_code[v >> 4], s_code[v & 15]);
-        val = *reinterpret_cast<uint32_t*>(&h);
+        w0 = w1 = *reinterpret_cast<uint32_t*>(&h);
       } else {
-        val = __float_as_uint((j & 1) ? s_code[v & 15] : s_code[v >> 4]);
+        w0 = __float_as_uint(s_code[v >> 4]);
+        w1 = __float_as_uint(s_code[v & 15]);
       }
-      asm volatile("st.shared.b32 [%0], %1;" ::"r"(kLutWin + v * 256 + j * 4), "r"(val));
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(kLutWin + v * 256 + q * 16),
+                   "r"(w0), "r"(w1), "r"(w0), "r"(w1));
     }
   }
   __syncthreads();
@@ -734,63 +737,108 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
 
 // Routing of the layer's single token, identical in every CTA.
 struct RouteSmem {
-  route::FF part[kWarpsK];
+  double part[kWarpsK * MOE_MAX_EXPERTS];
   float w[8];          // routing weights in top-k output order
   int64_t idx[8];      // routed experts in top-k output order
   float w_slot[8];     // weight of the pair at sorted position p (ascending expert id)
   int32_t zero_tok[8];  // every pair reads token row 0
 };
 
-// Logits by the exact double-float gate dot products (warp w: expert w % E,
-// range w / E of the row), softmax and top-k as the router kernels; then the
-// counting sort of the k pairs by expert (offsets, active experts).
-__device__ __forceinline__ Active route_token(const DecodeArgs& a, int* s_off, int* s_active,
-                                              RouteSmem& rs) {
+// Routing split: thread i takes the row's 16-byte vectors i, i + 512, ... and
+// accumulates every expert from each (one load of the token per CTA).  The
+// weights of its first vector for experts < kRoutePre are loaded before the
+// wait on the predecessor (the gate weights do not depend on it).
+constexpr int kRoutePre = 8;
+__device__ __forceinline__ void route_preload(const DecodeArgs& a, uint4 (&wpre)[kRoutePre]) {
+  const int nvec = a.H >> 3, v = threadIdx.x;
+  const uint4* wg = reinterpret_cast<const uint4*>(a.route_wg);
+#pragma unroll
+  for (int e = 0; e < kRoutePre; ++e)
+    wpre[e] = (e < a.E && v < nvec) ? __ldg(wg + (int64_t)e * nvec + v) : make_uint4(0, 0, 0, 0);
+}
+
+// acc += sum of the 8 exact fp16 x fp16 products of one vector (FP64 FMA:
+// each product is exact in double, each add rounds to 53 bits).
+__device__ __forceinline__ void dot8_f64(double& acc, const double (&hd)[8], const uint4& wv) {
+  const __half2* ww = reinterpret_cast<const __half2*>(&wv);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 y = __half22float2(ww[q]);
+    acc = fma((double)y.x, hd[2 * q], acc);
+    acc = fma((double)y.y, hd[2 * q + 1], acc);
+  }
+}
+
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Logits as the FP64 sum of the exact fp16 products (each thread sums its
+// vectors in ascending order, then lanes by butterfly, then warps in order),
+// rounded once to fp16 -- the correctly rounded logit, as the router kernels
+// and a float64 matmul give; softmax and top-k as the router kernels; then
+// the counting sort of the k pairs by expert (offsets, active experts).  The
+// code runs once per launch, so it is kept short (cold instruction fetch).
+__device__ __forceinline__ Active route_token(const DecodeArgs& a, const uint4 (&wpre)[kRoutePre],
+                                              int* s_off, int* s_active, RouteSmem& rs) {
   __shared__ int s_n;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int E = a.E, k = a.route_k, H = a.H;
   const int nvec = H >> 3;
-  const int groups = kWarpsK / E;  // >= 1 (E <= 16)
-  if (warp < groups * E) {
-    const int e = warp % E, r = warp / E;
-    const int v0 = nvec * r / groups, v1 = nvec * (r + 1) / groups;
-    const uint4* hrow = reinterpret_cast<const uint4*>(a.x);
-    const uint4* wrow = reinterpret_cast<const uint4*>(a.route_wg) + (int64_t)e * nvec;
-    route::FF acc{0.f, 0.f};
-    constexpr int U = 4;
-    for (int vb = v0 + lane; vb < v1; vb += 32 * U) {
-      uint4 hv[U], wv[U];
+  const uint4* hrow = reinterpret_cast<const uint4*>(a.x);
+  const uint4* wg = reinterpret_cast<const uint4*>(a.route_wg);
+  double acc[kRoutePre];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int v = vb + u * 32;
-        hv[u] = v < v1 ? hrow[v] : make_uint4(0, 0, 0, 0);
-        wv[u] = v < v1 ? __ldg(wrow + v) : make_uint4(0, 0, 0, 0);
-      }
+  for (int e = 0; e < kRoutePre; ++e) acc[e] = 0.0;
+  double* part = rs.part;  // [kWarpsK][MOE_MAX_EXPERTS]
+  for (int v = threadIdx.x; v < nvec; v += kThreadsK) {
+    const uint4 hv = hrow[v];
+    const __half2* hh = reinterpret_cast<const __half2*>(&hv);
+    double hd[8];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const __half2* hh = reinterpret_cast<const __half2*>(&hv[u]);
-        const __half2* ww = reinterpret_cast<const __half2*>(&wv[u]);
+    for (int q = 0; q < 4; ++q) {
+      const float2 x = __half22float2(hh[q]);
+      hd[2 * q] = x.x;
+      hd[2 * q + 1] = x.y;
+    }
+    const bool first = v == threadIdx.x;
+#pragma unroll
+    for (int e = 0; e < kRoutePre; ++e)
+      if (e < E) dot8_f64(acc[e], hd, first ? wpre[e] : __ldg(wg + (int64_t)e * nvec + v));
+  }
+#pragma unroll 1
+  for (int e = 0; e < E; ++e) {
+    double tot = 0.0;
+    if (e < kRoutePre) {
+#pragma unroll
+      for (int j = 0; j < kRoutePre; ++j)
+        if (j == e) tot = acc[j];
+    } else {  // experts past the preloaded ones: one more pass over the row
+      double hd[8];
+      for (int v = threadIdx.x; v < nvec; v += kThreadsK) {
+        const uint4 hv = hrow[v];
+        const __half2* hh = reinterpret_cast<const __half2*>(&hv);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float2 x = __half22float2(hh[q]), y = __half22float2(ww[q]);
-          route::ff_add(acc, __fmul_rn(x.x, y.x));
-          route::ff_add(acc, __fmul_rn(x.y, y.y));
+          const float2 x = __half22float2(hh[q]);
+          hd[2 * q] = x.x;
+          hd[2 * q + 1] = x.y;
         }
+        dot8_f64(tot, hd, __ldg(wg + (int64_t)e * nvec + v));
       }
     }
-    const route::FF tot = route::warp_sum_ff(acc);
-    if (lane == 0) rs.part[warp] = tot;
+    tot = warp_sum_f64(tot);
+    if (lane == 0) part[warp * MOE_MAX_EXPERTS + e] = tot;
   }
   __syncthreads();
   if (warp == 0) {
     int W = 1;
     while (W < E) W <<= 1;
     double mine = 0.0;
-    if (lane < E) {
-      route::FF tot = rs.part[lane];
-      for (int r = 1; r < groups; ++r) route::ff_merge(tot, rs.part[r * E + lane]);
-      mine = route::ff_value(tot);
-    }
+    if (lane < E)
+      for (int w = 0; w < kWarpsK; ++w) mine += rs.part[w * MOE_MAX_EXPERTS + lane];
     route::finish_token(mine, lane, E, W, k, 0, nullptr, rs.w, rs.idx);
     __syncwarp();
     // Stable counting sort of the k pairs (distinct experts) by expert id.
@@ -829,7 +877,7 @@ template <bool kMulti>
 __device__ __forceinline__ void combine_rows(const DecodeArgs& a, const Active& act,
                                              const RouteSmem& rs) {
   constexpr int kRows = 16 * down_tiles<kMulti>();
-  constexpr int kChunk = 64;
+  constexpr int kChunk = kThreadsK;
   __shared__ int s_won[kChunk];
   __shared__ int s_nwon;
   const int groups = a.H / kRows, per = a.S * groups;
@@ -838,17 +886,17 @@ __device__ __forceinline__ void combine_rows(const DecodeArgs& a, const Active& 
   const int target = act.n * a.S;
   const int k = a.route_k, S = a.S, H = a.H;
   for (int c0 = first; c0 < last; c0 += kChunk) {
-    const int c1 = min(last, c0 + kChunk);
+    if (threadIdx.x == 0) s_nwon = 0;
     __syncthreads();  // this CTA's y_part stores (and the previous chunk's reads) are done
-    if (threadIdx.x == 0) {
+    // One item per thread: release, count, and on the last count acquire.
+    const int i = c0 + threadIdx.x;
+    if (i < last) {
+      const int rg = (i % per) % groups;
       fence_release_gpu();
-      int nw = 0;
-      for (int i = c0; i < c1; ++i) {
-        const int rg = (i % per) % groups;
-        if (atomicAdd(a.rg_count + rg, 1) == target - 1) s_won[nw++] = rg;
+      if (atomicAdd(a.rg_count + rg, 1) == target - 1) {
+        fence_release_gpu();  // acquire side: the other CTAs' partials of this group
+        s_won[atomicAdd(&s_nwon, 1)] = rg;
       }
-      fence_release_gpu();  // acquire side: the other CTAs' partials of won groups
-      s_nwon = nw;
     }
     __syncthreads();
     const int nw = s_nwon;
@@ -863,6 +911,7 @@ __device__ __forceinline__ void combine_rows(const DecodeArgs& a, const Active& 
       }
       a.out[c] = f2h(acc);
     }
+    __syncthreads();
   }
 }
 
@@ -892,12 +941,14 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_stage_mma(const __grid_constan
   // full-grid kernel (nothing to overlap) and first checks it has work.
   __shared__ RouteSmem s_route;
   pdl_trigger();
+  const bool routed = !kMulti && a.route_wg != nullptr;
+  uint4 wpre[kRoutePre];
+  if (routed) route_preload(a, wpre);
   const bool room = smem_u32(smem) + red_floats<kMulti>() * 4 <= kLutWin;
   bool lut_ok = !kMulti && room && build_lut(a.ex.e[0].w1.code, smem);
   pdl_wait();
-  const bool routed = !kMulti && a.route_wg != nullptr;
-  const Active act =
-      routed ? route_token(a, s_off, s_active, s_route) : load_active<kMulti>(a, s_off, s_active);
+  const Active act = routed ? route_token(a, wpre, s_off, s_active, s_route)
+                            : load_active<kMulti>(a, s_off, s_active);
   if (act.n == 0) return;
   if (kMulti) lut_ok = room && build_lut(a.ex.e[0].w1.code, smem);
   if (!lut_ok) return;
