@@ -174,11 +174,33 @@ def expert_array(descs: Sequence[NF4Expert]):
     return arr
 
 
+# Decode-sized layer calls reuse one workspace (and routing scratch) per
+# (device, stream, shape): calls on one stream are ordered, and every kernel
+# of the layer waits for its predecessor before it touches the workspace.
+_DECODE_WS_MAX_TOKENS = 8
+_layer_ws: dict = {}
+
+
+def _layer_scratch(dev: torch.device, stream: int, T: int, hidden: int, inter: int, E: int, k: int):
+    key = (dev.index, stream, T, hidden, inter, E, k)
+    ent = _layer_ws.get(key)
+    if ent is None:
+        ws_bytes = _native.lib().moe_layer_workspace_size(T, hidden, inter, E, k)
+        ent = (_workspace(ws_bytes, dev), ws_bytes,
+               torch.empty(T, k, dtype=torch.int64, device=dev),
+               torch.empty(T, k, dtype=torch.float32, device=dev))
+        if T <= _DECODE_WS_MAX_TOKENS:
+            _layer_ws[key] = ent
+    return ent
+
+
 def layer_forward(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hidden: int, inter: int,
-                  out: torch.Tensor | None = None):
+                  out: torch.Tensor | None = None, routing: bool = True):
     """Fused MoE layer: returns ``(out fp16 [T,H], indices int64 [T,k], weights fp32 [T,k])``.
 
     ``experts`` is a ctypes array of ``NF4Expert`` (see :func:`expert_array`).
+    ``routing=False``: the caller discards indices and weights (returned as
+    None; the kernels write them to reused scratch).
     """
     dev = _need_cuda("layer_forward", h=h, wg=wg)
     _need_dtype("layer_forward", h, torch.float16, "hidden_states")
@@ -187,14 +209,15 @@ def layer_forward(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hidden: in
     E = len(experts)
     if out is None:
         out = torch.empty(T, hidden, dtype=torch.float16, device=dev)
-    idx = torch.empty(T, k, dtype=torch.int64, device=dev)
-    w = torch.empty(T, k, dtype=torch.float32, device=dev)
-    lib = _native.lib()
-    ws_bytes = lib.moe_layer_workspace_size(T, hidden, inter, E, k)
-    ws = _workspace(ws_bytes, dev)
-    check(lib.moe_layer_forward(_p(h), _p(wg), experts, E, k, T, hidden, inter, _p(out), _p(idx),
-                                _p(w), _p(ws), ws_bytes, _stream(dev)), "moe_layer_forward")
-    return out, idx, w
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    ws, ws_bytes, idx, w = _layer_scratch(dev, stream, T, hidden, inter, E, k)
+    if routing:
+        idx = torch.empty(T, k, dtype=torch.int64, device=dev)
+        w = torch.empty(T, k, dtype=torch.float32, device=dev)
+    check(_native.lib().moe_layer_forward(_p(h), _p(wg), experts, E, k, T, hidden, inter, _p(out),
+                                          _p(idx), _p(w), _p(ws), ws_bytes,
+                                          ctypes.c_void_p(stream)), "moe_layer_forward")
+    return (out, idx, w) if routing else (out, None, None)
 
 
 def layer_forward_noalloc(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hidden: int,

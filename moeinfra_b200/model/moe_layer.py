@@ -120,7 +120,8 @@ class MoELayer:
     def _fused(self, hidden_states: torch.Tensor, table, inter: int) -> torch.Tensor:
         router = self.router
         out, _, _ = kernels.layer_forward(hidden_states.contiguous(), router.gate_f16(), table,
-                                          router.num_experts_per_tok, router.hidden_size, inter)
+                                          router.num_experts_per_tok, router.hidden_size, inter,
+                                          routing=False)
         return out
 
     # -- forward -------------------------------------------------------------------
