@@ -15,10 +15,11 @@ Arms:
 * default (this build): ``value`` = tokens/s of the device-timed step (CUDA
   graph of the 32 layers' fused kernels, inputs resident); ``e2e`` = the same
   tokens/s through the public API (``MoELayer.forward`` per layer, eager) with
-  the step's tokens copied from pinned host memory and all 32 layer outputs
-  read back to pinned host memory every step; ``roofline`` from the expert stage
-  (``moe_experts_forward``: gate/up GEMV + SwiGLU, down GEMV, split reduce)
-  timed on its own with CUDA events; ``cpu_baseline`` from the CPU restatement
+  the step's tokens copied from pinned host memory and the step's result (the
+  last layer's output) read back to pinned host memory every step; ``roofline``
+  from the expert stage (``moe_experts_forward``: the fused gate/up + SwiGLU and
+  down GEMV kernel, then the split reduce) timed on its own with CUDA events;
+  ``cpu_baseline`` from the CPU restatement
   (``oracle.cpu_path``) on a bounded sample.
 * ``--impl reference``: the CPU restatement of the reference's path timed on
   the host cores (bitsandbytes, which the reference's CPU path needs, is not
@@ -403,8 +404,9 @@ def run_device(args, rank: int, world: int, local_rank: int):
         traffic = _profile_traffic()
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak[0], "unit": "GB/s",
                 "frac": round(achieved / peak[0], 4), "traffic": traffic,
-                "kernel": "expert stage (moe_experts_forward: gate/up GEMV+SwiGLU, down GEMV, "
-                          "split reduce), bs1, per layer",
+                "kernel": "expert stage (moe_experts_forward: k_stage_mma, one launch for the "
+                          "W1/W3 GEMV+SwiGLU and the W2 split-K GEMV, then the split reduce), "
+                          "bs1, per layer",
                 "algorithmic_bytes_per_launch": int(bytes_per_launch),
                 "launch_us": round(per_launch_s * 1e6, 2), "peak_source": peak[1]}
         del g2
