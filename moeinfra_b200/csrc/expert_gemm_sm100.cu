@@ -13,7 +13,7 @@
 //   down   : D = W2 . H^T (256 columns), epilogue y = fp16(D) -> y_sorted [P, H].
 // Warp roles (320 threads):
 //   warps 0-7  dequantize the 128 x 64 weight tile of each K step (one NF4
-//              block per row; warp w takes rows 32*(w%4).., byte half w/4)
+//              block per row; warp w takes rows 32*(w%4).., byte part w/4)
 //              straight into shared memory in the UMMA K-major 128-byte
 //              swizzled layout, then run the epilogue (TMEM -> registers ->
 //              global);
@@ -38,9 +38,12 @@ constexpr int kBM = 128;           // weight rows per tile (UMMA M)
 constexpr int kBK = 64;            // K per stage: one NF4 block
 constexpr int kMaxN = 256;         // tokens per tile (UMMA N, max)
 constexpr int kBoxRows = 64;       // token rows per TMA box
-constexpr int kDqWarps = 8;
-constexpr int kPrefetch = 4;       // K steps of packed weights in flight per dequant thread
-constexpr int kThreads = (kDqWarps + 2) * 32;
+// Dequant warps per CTA: 8 when the tiles are wide (prefill: shared-memory
+// bandwidth bounds, more warps do not help), 16 when they are narrow (decode
+// batches of ~16 tokens per expert: the dequant arithmetic bounds).  Warp w
+// takes rows 32*(w%4).. and part w/4 of the row's 32 packed bytes.
+template <int DQ>
+constexpr int threads_for() { return (DQ + 2) * 32; }
 constexpr uint32_t kATile = kBM * kBK * 2;         // 16 KB fp16, swizzled
 constexpr uint32_t kBBox = kBoxRows * kBK * 2;      // 8 KB
 constexpr uint32_t kBTile = kMaxN * kBK * 2;        // 32 KB
@@ -49,11 +52,16 @@ constexpr long long kWaitCycles = 4000000000LL;     // ~2 s at 2 GHz
 
 __device__ int g_gemm_error = 0;
 
-template <bool kGate>
+// kNarrow: tiles of at most 64 tokens (one TMA box), whose token slot is a
+// quarter of the wide one, so more stages fit and hide the per-stage hand-off.
+template <bool kGate, bool kNarrow>
 struct Cfg {
   static constexpr int kMats = kGate ? 2 : 1;
-  static constexpr int kStages = kGate ? 3 : 4;
-  static constexpr uint32_t kStage = kMats * kATile + kBTile;
+  static constexpr int kTileN = kNarrow ? kBoxRows : kMaxN;
+  static constexpr int kStages = kNarrow ? (kGate ? 4 : 8) : (kGate ? 3 : 4);
+  // K steps of packed codes in flight per dequant thread.
+  static constexpr int kPrefetch = kNarrow ? (kGate ? 6 : 8) : 4;
+  static constexpr uint32_t kStage = kMats * kATile + (uint32_t)kTileN * kBK * 2;
   static constexpr uint32_t kTmemCols = kGate ? 512 : 256;
   static constexpr uint32_t kSmem = kStages * kStage + kLutBytes + 1024;  // + alignment slack
 };
@@ -200,23 +208,28 @@ __device__ __forceinline__ uint32_t instr_desc(int n) {
 struct Tile {
   int e, m0, n0, nt;
 };
+template <int kTileN>
 __device__ __forceinline__ Tile tile_of(int t, const int* s_base, const int* s_off, int E,
                                         int mtiles) {
   int e = 0;
   while (e + 1 < E && s_base[e + 1] <= t) ++e;
   const int local = t - s_base[e];
   const int n_e = s_off[e + 1] - s_off[e];
-  const int nch = (n_e + kMaxN - 1) / kMaxN;
+  const int nch = (n_e + kTileN - 1) / kTileN;
   const int m = local / nch, c = local - m * nch;
-  const int n0 = c * kMaxN;
-  const int nt = min(kMaxN, n_e - n0);
+  const int n0 = c * kTileN;
+  const int nt = min(kTileN, n_e - n0);
   return Tile{e, m * kBM, n0, nt};
 }
 
-template <bool kGate>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool kGate, int kDqWarps>
+__global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
     k_grouped_gemm(const __grid_constant__ GemmArgs a, const __grid_constant__ CUtensorMap tmap) {
-  using C = Cfg<kGate>;
+  using C = Cfg<kGate, kDqWarps == 16>;
+  constexpr int kPrefetch = C::kPrefetch;
+  constexpr int kThreads = threads_for<kDqWarps>();
+  constexpr int kParts = kDqWarps / 4;  // parts of a row's 32 packed bytes
+  constexpr int kWords = 8 / kParts;    // 4-byte words of codes per thread per K step
   constexpr int NS = C::kStages;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ __align__(8) unsigned long long s_afull[NS], s_bfull[NS], s_empty[NS];
@@ -240,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int e = 0; e < a.E; ++e) {
       s_base[e] = acc;
       const int n = s_off[e + 1] - s_off[e];
-      acc += n > 0 ? mtiles * ((n + kMaxN - 1) / kMaxN) : 0;
+      acc += n > 0 ? mtiles * ((n + C::kTileN - 1) / C::kTileN) : 0;
     }
     s_base[a.E] = acc;
     s_abort = 0;
@@ -279,34 +292,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < kDqWarps) {
     // ---------------- dequant producers + epilogue ----------------
-    const int half = warp / 4, rw = warp % 4;
+    const int part = warp / 4, rw = warp % 4;
     const int i = rw * 32 + lane;  // tile row (also TMEM lane)
     const uint32_t lut_lane = lut + (lane & 15) * 8;
     uint32_t g = 0, it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
-      const Tile tl = tile_of(t, s_base, s_off, a.E, mtiles);
+      const Tile tl = tile_of<C::kTileN>(t, s_base, s_off, a.E, mtiles);
       const moe_nf4_expert_t& ex = a.ex.e[tl.e];
       const moe_nf4_matrix_t* mats[2] = {kGate ? &ex.w1 : &ex.w2, &ex.w3};
       const int R = tl.m0 + i;
       const int64_t rowseg = (int64_t)(R >> 4) * nblk * 16 + (R & 15);
-      // This thread's 16 bytes of block 0 and its absmax; block kb is 512 bytes
-      // (16 floats) further on in tile16.
-      const uint4* qp[C::kMats];
+      // This thread's 4*kWords bytes of block 0 and its absmax; block kb is 512
+      // bytes (16 floats) further on in tile16.
+      const uint8_t* qp[C::kMats];
       const float* ap[C::kMats];
 #pragma unroll
       for (int m = 0; m < C::kMats; ++m) {
-        qp[m] = reinterpret_cast<const uint4*>(mats[m]->q + rowseg * 32 + half * 16);
+        qp[m] = mats[m]->q + rowseg * 32 + part * (4 * kWords);
         ap[m] = mats[m]->absmax + rowseg;
       }
       // Packed codes and absmax of K steps kb .. kb+kPrefetch-1 in flight in
       // registers while step kb is decoded.
-      uint4 qv[kPrefetch][C::kMats];
+      uint32_t qv[kPrefetch][C::kMats][kWords];
       float av[kPrefetch][C::kMats];
-      auto load = [&](int kb, uint4* q, float* am) {
+      auto load = [&](int kb, uint32_t (*q)[kWords], float* am) {
         if (kb < nblk) {
 #pragma unroll
           for (int m = 0; m < C::kMats; ++m) {
-            q[m] = __ldg(qp[m] + (int64_t)kb * 32);
+            const uint8_t* src = qp[m] + (int64_t)kb * 512;
+            if constexpr (kWords == 4) {
+              const uint4 v = __ldg(reinterpret_cast<const uint4*>(src));
+              q[m][0] = v.x; q[m][1] = v.y; q[m][2] = v.z; q[m][3] = v.w;
+            } else {
+              const uint2 v = __ldg(reinterpret_cast<const uint2*>(src));
+              q[m][0] = v.x; q[m][1] = v.y;
+            }
             am[m] = __ldg(ap[m] + (int64_t)kb * 16);
           }
         }
@@ -329,16 +349,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t stage = base + s * C::kStage;
 #pragma unroll
           for (int m = 0; m < C::kMats; ++m) {
-            const uint32_t w[4] = {qv[d][m].x, qv[d][m].y, qv[d][m].z, qv[d][m].w};
             const uint32_t amb = __float_as_uint(av[d][m]);
             const uint64_t am2 = (static_cast<uint64_t>(amb) << 32) | amb;
             const uint32_t arow = stage + m * kATile + (i >> 3) * 1024 + (i & 7) * 128;
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = 0; cc < kWords; ++cc) {
               uint32_t h[4];
 #pragma unroll
-              for (int b = 0; b < 4; ++b) h[b] = decode_byte(w[cc], 8 * b, lut_lane, am2);
-              const int chunk = half * 4 + cc;
+              for (int b = 0; b < 4; ++b) h[b] = decode_byte(qv[d][m][cc], 8 * b, lut_lane, am2);
+              const int chunk = part * kWords + cc;
               asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
                                arow + ((chunk ^ (i & 7)) << 4)),
                            "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
@@ -362,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int nchunk = (tl.nt + 15) / 16;
       const uint32_t lane_addr = tmem + ((uint32_t)(rw * 32) << 16);
-      for (int ch = half; ch < nchunk; ch += 2) {
+      for (int ch = part; ch < nchunk; ch += kParts) {
         uint32_t d1[16], d3[16];
         tmem_ld16(lane_addr + ch * 16, d1);
         if (kGate) tmem_ld16(lane_addr + 256 + ch * 16, d3);
@@ -391,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t g = 0;
       for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x) {
-        const Tile tl = tile_of(t, s_base, s_off, a.E, mtiles);
+        const Tile tl = tile_of<C::kTileN>(t, s_base, s_off, a.E, mtiles);
         const int nbox = (tl.nt + kBoxRows - 1) / kBoxRows;
         const int row0 = s_off[tl.e] + tl.n0;
         for (int kb = 0; kb < nblk; ++kb, ++g) {
@@ -416,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0, it = 0;
       bool issued_any = false;
       for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x, ++it) {
-        const Tile tl = tile_of(t, s_base, s_off, a.E, mtiles);
+        const Tile tl = tile_of<C::kTileN>(t, s_base, s_off, a.E, mtiles);
         const int n = (tl.nt + 15) & ~15;
         const uint32_t idesc = instr_desc(n);
         if (!mbar_wait(saddr(&s_accempty), (it & 1) ^ 1)) {
@@ -495,17 +514,24 @@ bool make_token_map(CUtensorMap* map, const uint16_t* x, int64_t rows_total, int
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool kGate>
-int launch_one(const GemmArgs& a, const uint16_t* x, int64_t P, cudaStream_t s) {
-  static bool attr = cudaFuncSetAttribute(k_grouped_gemm<kGate>,
+template <bool kGate, int DQ>
+int launch_dq(const GemmArgs& a, const CUtensorMap& map, cudaStream_t s) {
+  static bool attr = cudaFuncSetAttribute(k_grouped_gemm<kGate, DQ>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          Cfg<kGate>::kSmem) == cudaSuccess;
+                                          Cfg<kGate, DQ == 16>::kSmem) == cudaSuccess;
   if (!attr) return MOE_ERR_CUDA;
-  CUtensorMap map;
-  if (!make_token_map(&map, x, P, a.K)) return MOE_ERR_CUDA;
-  k_grouped_gemm<kGate><<<sm_count(), kThreads, Cfg<kGate>::kSmem, s>>>(a, map);
+  k_grouped_gemm<kGate, DQ><<<sm_count(), threads_for<DQ>(), Cfg<kGate, DQ == 16>::kSmem, s>>>(a, map);
   MOE_CHECK_LAUNCH();
   return MOE_OK;
+}
+
+// Narrow tiles (on average at most 64 tokens per expert): 16 dequant warps,
+// 64-token tiles (an expert with more tokens takes several), deeper pipeline.
+template <bool kGate>
+int launch_one(const GemmArgs& a, const uint16_t* x, int64_t P, cudaStream_t s) {
+  CUtensorMap map;
+  if (!make_token_map(&map, x, P, a.K)) return MOE_ERR_CUDA;
+  return P <= (int64_t)64 * a.E ? launch_dq<kGate, 16>(a, map, s) : launch_dq<kGate, 8>(a, map, s);
 }
 
 }  // namespace
