@@ -54,16 +54,27 @@ __device__ int g_gemm_error = 0;
 
 // kNarrow: tiles of at most 64 tokens (one TMA box), whose token slot is a
 // quarter of the wide one, so more stages fit and hide the per-stage hand-off.
+// Narrow tiles also keep the dequantized weights (A) in tensor memory: the
+// dequant threads (one weight row each) write them with tcgen05.st and the
+// MMA reads A from TMEM, so A never crosses shared memory (at ~16 tokens per
+// expert the shared-memory traffic of A bounded the kernel).  TMEM columns:
+// accumulators (W1 at 0, W3 at kTileN), then the A stages, 32 columns per
+// matrix and stage.
 template <bool kGate, bool kNarrow>
 struct Cfg {
   static constexpr int kMats = kGate ? 2 : 1;
   static constexpr int kTileN = kNarrow ? kBoxRows : kMaxN;
-  static constexpr int kStages = kNarrow ? (kGate ? 4 : 8) : (kGate ? 3 : 4);
+  static constexpr bool kATmem = kNarrow;
+  static constexpr int kStages = kNarrow ? (kGate ? 6 : 8) : (kGate ? 3 : 4);
   // K steps of packed codes in flight per dequant thread.
   static constexpr int kPrefetch = kNarrow ? (kGate ? 6 : 8) : 4;
-  static constexpr uint32_t kStage = kMats * kATile + (uint32_t)kTileN * kBK * 2;
-  static constexpr uint32_t kTmemCols = kGate ? 512 : 256;
+  static constexpr uint32_t kAStage = kATmem ? 0 : kMats * kATile;  // A bytes in a smem stage
+  static constexpr uint32_t kStage = kAStage + (uint32_t)kTileN * kBK * 2;
+  static constexpr uint32_t kDCol3 = kNarrow ? kTileN : 256;       // W3 accumulator column
+  static constexpr uint32_t kACol = kNarrow ? kMats * kTileN : 0;  // first A column
+  static constexpr uint32_t kTmemCols = (kGate || kNarrow) ? 512 : 256;
   static constexpr uint32_t kSmem = kStages * kStage + kLutBytes + 1024;  // + alignment slack
+  static_assert(!kATmem || kACol + kStages * kMats * 32 <= kTmemCols, "TMEM columns");
 };
 
 struct GemmArgs {
@@ -191,6 +202,28 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
 }
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// D[tmem] (+)= A[tmem] . B[smem desc]^T, kind::f16: A is 128 lanes (rows) x 8
+// columns (16 fp16 of K, the lower K index in the lower half of a column).
+__device__ __forceinline__ void tc_mma_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+      : "memory");
+}
+// Each thread of the warp writes 8 consecutive columns of its own lane.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
@@ -347,24 +380,43 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
             break;
           }
           const uint32_t stage = base + s * C::kStage;
+          if constexpr (C::kATmem) tc_fence_after();  // the MMA that read this stage is done
 #pragma unroll
           for (int m = 0; m < C::kMats; ++m) {
             const uint32_t amb = __float_as_uint(av[d][m]);
             const uint64_t am2 = (static_cast<uint64_t>(amb) << 32) | amb;
-            const uint32_t arow = stage + m * kATile + (i >> 3) * 1024 + (i & 7) * 128;
+            if constexpr (C::kATmem) {
+              static_assert(kWords == 2, "TMEM A: 8 columns per thread");
+              uint32_t h[8];
 #pragma unroll
-            for (int cc = 0; cc < kWords; ++cc) {
-              uint32_t h[4];
+              for (int cc = 0; cc < kWords; ++cc)
 #pragma unroll
-              for (int b = 0; b < 4; ++b) h[b] = decode_byte(qv[d][m][cc], 8 * b, lut_lane, am2);
-              const int chunk = part * kWords + cc;
-              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                               arow + ((chunk ^ (i & 7)) << 4)),
-                           "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
-                           : "memory");
+                for (int b = 0; b < 4; ++b)
+                  h[cc * 4 + b] = decode_byte(qv[d][m][cc], 8 * b, lut_lane, am2);
+              tmem_st8(tmem + ((uint32_t)(rw * 32) << 16) + C::kACol + (s * C::kMats + m) * 32 +
+                           part * 8,
+                       h);
+            } else {
+              const uint32_t arow = stage + m * kATile + (i >> 3) * 1024 + (i & 7) * 128;
+#pragma unroll
+              for (int cc = 0; cc < kWords; ++cc) {
+                uint32_t h[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) h[b] = decode_byte(qv[d][m][cc], 8 * b, lut_lane, am2);
+                const int chunk = part * kWords + cc;
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                 arow + ((chunk ^ (i & 7)) << 4)),
+                             "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
+                             : "memory");
+              }
             }
           }
-          fence_proxy_async();
+          if constexpr (C::kATmem) {
+            tmem_wait_st();
+            tc_fence_before();
+          } else {
+            fence_proxy_async();
+          }
           __syncwarp();
           if ((threadIdx.x & 31) == 0) mbar_arrive(saddr(&s_afull[s]));
           ++g;
@@ -384,7 +436,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
       for (int ch = part; ch < nchunk; ch += kParts) {
         uint32_t d1[16], d3[16];
         tmem_ld16(lane_addr + ch * 16, d1);
-        if (kGate) tmem_ld16(lane_addr + 256 + ch * 16, d3);
+        if (kGate) tmem_ld16(lane_addr + C::kDCol3 + ch * 16, d3);
         tmem_wait_ld();
         const int row = tl.m0 + i;
 #pragma unroll
@@ -418,7 +470,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
           if (!s_abort && !mbar_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1)) s_abort = 1;
           if (s_abort) break;
           const uint32_t bar = saddr(&s_bfull[s]);
-          const uint32_t bt = base + s * C::kStage + C::kMats * kATile;
+          const uint32_t bt = base + s * C::kStage + C::kAStage;
           mbar_expect_tx(bar, nbox * kBBox);
           for (int bx = 0; bx < nbox; ++bx)
             tma_load_2d(bt + bx * kBBox, &tmap, bar, kb * kBK, row0 + bx * kBoxRows);
@@ -452,13 +504,18 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
           }
           tc_fence_after();
           const uint32_t stage = base + s * C::kStage;
-          const uint32_t bt = stage + C::kMats * kATile;
+          const uint32_t bt = stage + C::kAStage;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
 #pragma unroll
-            for (int m = 0; m < C::kMats; ++m)
-              tc_mma(tmem + m * 256, smem_desc(stage + m * kATile + kk * 32), smem_desc(bt + kk * 32),
-                     idesc, (kb | kk) != 0);
+            for (int m = 0; m < C::kMats; ++m) {
+              if constexpr (C::kATmem)
+                tc_mma_ta(tmem + m * C::kDCol3, tmem + C::kACol + (s * C::kMats + m) * 32 + kk * 8,
+                          smem_desc(bt + kk * 32), idesc, (kb | kk) != 0);
+              else
+                tc_mma(tmem + m * C::kDCol3, smem_desc(stage + m * kATile + kk * 32),
+                       smem_desc(bt + kk * 32), idesc, (kb | kk) != 0);
+            }
           }
           issued_any = true;
           tc_commit(saddr(&s_empty[s]));
