@@ -48,6 +48,10 @@ constexpr uint32_t kATile = kBM * kBK * 2;         // 16 KB fp16, swizzled
 constexpr uint32_t kBBox = kBoxRows * kBK * 2;      // 8 KB
 constexpr uint32_t kBTile = kMaxN * kBK * 2;        // 32 KB
 constexpr uint32_t kLutBytes = 256 * 16 * 8;        // byte -> (code hi, code lo), 16 replicas
+// Narrow tiles: the table (32 replicas, 64 KB) sits at shared-window address
+// 0x10000, entry (byte v, lane l) at 0x10000 | v << 8 | l * 8, so one byte
+// permute of the packed word forms the address.
+constexpr uint32_t kLutWin = 0x10000;
 constexpr long long kWaitCycles = 4000000000LL;     // ~2 s at 2 GHz
 
 __device__ int g_gemm_error = 0;
@@ -65,7 +69,7 @@ struct Cfg {
   static constexpr int kMats = kGate ? 2 : 1;
   static constexpr int kTileN = kNarrow ? kBoxRows : kMaxN;
   static constexpr bool kATmem = kNarrow;
-  static constexpr int kStages = kNarrow ? (kGate ? 6 : 8) : (kGate ? 3 : 4);
+  static constexpr int kStages = kNarrow ? (kGate ? 6 : 7) : (kGate ? 3 : 4);
   // K steps of packed codes in flight per dequant thread.
   static constexpr int kPrefetch = kNarrow ? (kGate ? 6 : 8) : 4;
   static constexpr uint32_t kAStage = kATmem ? 0 : kMats * kATile;  // A bytes in a smem stage
@@ -73,7 +77,12 @@ struct Cfg {
   static constexpr uint32_t kDCol3 = kNarrow ? kTileN : 256;       // W3 accumulator column
   static constexpr uint32_t kACol = kNarrow ? kMats * kTileN : 0;  // first A column
   static constexpr uint32_t kTmemCols = (kGate || kNarrow) ? 512 : 256;
-  static constexpr uint32_t kSmem = kStages * kStage + kLutBytes + 1024;  // + alignment slack
+  static constexpr bool kLutWindow = kNarrow;
+  // Wide: stages, table, alignment slack.  Narrow: everything below the
+  // window (stages) plus the window itself.
+  static constexpr uint32_t kSmem =
+      kLutWindow ? 2 * kLutWin : kStages * kStage + kLutBytes + 1024;
+  static_assert(!kLutWindow || kStages * kStage + 8192 <= kLutWin, "stages below the table");
   static_assert(!kATmem || kACol + kStages * kMats * 32 <= kTmemCols, "TMEM columns");
 };
 
@@ -147,6 +156,23 @@ __device__ __forceinline__ uint32_t decode_byte(uint32_t w, uint32_t shift, uint
       " cvt.rn.f16x2.f32 %0, hi, lo;\n}\n"
       : "=r"(out)
       : "r"(w), "r"(shift), "r"(lut_lane), "l"(am2));
+  return out;
+}
+// The same for the windowed table: the address is one byte permute.
+template <int K>
+__device__ __forceinline__ uint32_t decode_byte_w(uint32_t w, uint32_t lut_lane, uint64_t am2) {
+  uint32_t out;
+  asm("{\n .reg .b32 ad, lo, hi, bf;\n .reg .b64 c, p;\n"
+      " prmt.b32 ad, %1, %2, %3;\n"
+      " ld.shared.b64 c, [ad];\n"
+      " mul.rn.f32x2 p, c, %4;\n"
+      " mov.b64 {lo, hi}, p;\n"
+      " cvt.rn.bf16x2.f32 bf, hi, lo;\n"
+      " and.b32 hi, bf, 0xFFFF0000;\n"
+      " shl.b32 lo, bf, 16;\n"
+      " cvt.rn.f16x2.f32 %0, hi, lo;\n}\n"
+      : "=r"(out)
+      : "r"(w), "r"(lut_lane), "n"(0x7604 | (K << 4)), "l"(am2));
   return out;
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -276,9 +302,13 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t raw = saddr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // stages: 1024-aligned (swizzle atoms)
-  const uint32_t lut = base + NS * C::kStage;
+  const uint32_t lut = C::kLutWindow ? kLutWin : base + NS * C::kStage;
   const int mtiles = a.rows / kBM;
   const int nblk = a.K / kBK;
+  if (C::kLutWindow && (base + NS * C::kStage > kLutWin || raw + C::kSmem < 2 * kLutWin)) {
+    if (threadIdx.x == 0) atomicExch(&g_gemm_error, 1);  // shared-memory layout not as planned
+    return;
+  }
 
   if (threadIdx.x == 0) {
     int acc = 0;
@@ -311,11 +341,20 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
   __syncthreads();
   // Byte -> (fp32 code of the high nibble, of the low nibble); 16 replicas so
   // the 16 lanes of a half-warp read disjoint banks.
-  for (int i = threadIdx.x; i < 256 * 16; i += kThreads) {
-    const int v = i >> 4;
-    float2 c = make_float2(s_code[v >> 4], s_code[v & 15]);
-    asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(lut + i * 8), "f"(c.x), "f"(c.y)
-                 : "memory");
+  if (C::kLutWindow) {
+    for (int i = threadIdx.x; i < 256 * 32; i += kThreads) {
+      const int v = i >> 5;
+      float2 c = make_float2(s_code[v >> 4], s_code[v & 15]);
+      asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(kLutWin + i * 8), "f"(c.x), "f"(c.y)
+                   : "memory");
+    }
+  } else {
+    for (int i = threadIdx.x; i < 256 * 16; i += kThreads) {
+      const int v = i >> 4;
+      float2 c = make_float2(s_code[v >> 4], s_code[v & 15]);
+      asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(lut + i * 8), "f"(c.x), "f"(c.y)
+                   : "memory");
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -327,7 +366,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
     // ---------------- dequant producers + epilogue ----------------
     const int part = warp / 4, rw = warp % 4;
     const int i = rw * 32 + lane;  // tile row (also TMEM lane)
-    const uint32_t lut_lane = lut + (lane & 15) * 8;
+    const uint32_t lut_lane = C::kLutWindow ? (kLutWin | (lane * 8)) : lut + (lane & 15) * 8;
     uint32_t g = 0, it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
       const Tile tl = tile_of<C::kTileN>(t, s_base, s_off, a.E, mtiles);
@@ -389,10 +428,12 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
               static_assert(kWords == 2, "TMEM A: 8 columns per thread");
               uint32_t h[8];
 #pragma unroll
-              for (int cc = 0; cc < kWords; ++cc)
-#pragma unroll
-                for (int b = 0; b < 4; ++b)
-                  h[cc * 4 + b] = decode_byte(qv[d][m][cc], 8 * b, lut_lane, am2);
+              for (int cc = 0; cc < kWords; ++cc) {
+                h[cc * 4 + 0] = decode_byte_w<0>(qv[d][m][cc], lut_lane, am2);
+                h[cc * 4 + 1] = decode_byte_w<1>(qv[d][m][cc], lut_lane, am2);
+                h[cc * 4 + 2] = decode_byte_w<2>(qv[d][m][cc], lut_lane, am2);
+                h[cc * 4 + 3] = decode_byte_w<3>(qv[d][m][cc], lut_lane, am2);
+              }
               tmem_st8(tmem + ((uint32_t)(rw * 32) << 16) + C::kACol + (s * C::kMats + m) * 32 +
                            part * 8,
                        h);
