@@ -58,25 +58,26 @@ __device__ int g_gemm_error = 0;
 
 // kNarrow: tiles of at most 64 tokens (one TMA box), whose token slot is a
 // quarter of the wide one, so more stages fit and hide the per-stage hand-off.
-// Narrow tiles also keep the dequantized weights (A) in tensor memory: the
-// dequant threads (one weight row each) write them with tcgen05.st and the
-// MMA reads A from TMEM, so A never crosses shared memory (at ~16 tokens per
-// expert the shared-memory traffic of A bounded the kernel).  TMEM columns:
+// Narrow tiles, and the down projection of wide ones, keep the dequantized
+// weights (A) in tensor memory: the dequant threads (one weight row each)
+// write them with tcgen05.st and the MMA reads A from TMEM, so A never crosses
+// shared memory (its shared-memory traffic bounded both).  TMEM columns:
 // accumulators (W1 at 0, W3 at kTileN), then the A stages, 32 columns per
-// matrix and stage.
+// matrix and stage.  Wide gate_up keeps A in shared memory: its two 256-column
+// accumulators fill TMEM.
 template <bool kGate, bool kNarrow>
 struct Cfg {
   static constexpr int kMats = kGate ? 2 : 1;
   static constexpr int kTileN = kNarrow ? kBoxRows : kMaxN;
-  static constexpr bool kATmem = kNarrow;
-  static constexpr int kStages = kNarrow ? (kGate ? 6 : 7) : (kGate ? 3 : 4);
+  static constexpr bool kATmem = kNarrow || !kGate;
+  static constexpr int kStages = kNarrow ? (kGate ? 6 : 7) : (kGate ? 3 : 6);
   // K steps of packed codes in flight per dequant thread.
   static constexpr int kPrefetch = kNarrow ? (kGate ? 6 : 8) : 4;
   static constexpr uint32_t kAStage = kATmem ? 0 : kMats * kATile;  // A bytes in a smem stage
   static constexpr uint32_t kStage = kAStage + (uint32_t)kTileN * kBK * 2;
   static constexpr uint32_t kDCol3 = kNarrow ? kTileN : 256;       // W3 accumulator column
-  static constexpr uint32_t kACol = kNarrow ? kMats * kTileN : 0;  // first A column
-  static constexpr uint32_t kTmemCols = (kGate || kNarrow) ? 512 : 256;
+  static constexpr uint32_t kACol = kATmem ? kMats * kTileN : 0;  // first A column
+  static constexpr uint32_t kTmemCols = 512;
   static constexpr bool kLutWindow = kNarrow;
   // Wide: stages, table, alignment slack.  Narrow: everything below the
   // window (stages) plus the window itself.
@@ -241,7 +242,15 @@ __device__ __forceinline__ void tc_mma_ta(uint32_t d_tmem, uint32_t a_tmem, uint
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
       : "memory");
 }
-// Each thread of the warp writes 8 consecutive columns of its own lane.
+// Each thread of the warp writes 8 (16) consecutive columns of its own lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
@@ -425,18 +434,26 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
             const uint32_t amb = __float_as_uint(av[d][m]);
             const uint64_t am2 = (static_cast<uint64_t>(amb) << 32) | amb;
             if constexpr (C::kATmem) {
-              static_assert(kWords == 2, "TMEM A: 8 columns per thread");
-              uint32_t h[8];
+              uint32_t h[kWords * 4];
 #pragma unroll
               for (int cc = 0; cc < kWords; ++cc) {
-                h[cc * 4 + 0] = decode_byte_w<0>(qv[d][m][cc], lut_lane, am2);
-                h[cc * 4 + 1] = decode_byte_w<1>(qv[d][m][cc], lut_lane, am2);
-                h[cc * 4 + 2] = decode_byte_w<2>(qv[d][m][cc], lut_lane, am2);
-                h[cc * 4 + 3] = decode_byte_w<3>(qv[d][m][cc], lut_lane, am2);
+                if constexpr (C::kLutWindow) {
+                  h[cc * 4 + 0] = decode_byte_w<0>(qv[d][m][cc], lut_lane, am2);
+                  h[cc * 4 + 1] = decode_byte_w<1>(qv[d][m][cc], lut_lane, am2);
+                  h[cc * 4 + 2] = decode_byte_w<2>(qv[d][m][cc], lut_lane, am2);
+                  h[cc * 4 + 3] = decode_byte_w<3>(qv[d][m][cc], lut_lane, am2);
+                } else {
+#pragma unroll
+                  for (int b = 0; b < 4; ++b)
+                    h[cc * 4 + b] = decode_byte(qv[d][m][cc], 8 * b, lut_lane, am2);
+                }
               }
-              tmem_st8(tmem + ((uint32_t)(rw * 32) << 16) + C::kACol + (s * C::kMats + m) * 32 +
-                           part * 8,
-                       h);
+              const uint32_t ta = tmem + ((uint32_t)(rw * 32) << 16) + C::kACol +
+                                  (s * C::kMats + m) * 32 + part * (kWords * 4);
+              if constexpr (kWords == 2)
+                tmem_st8(ta, h);
+              else
+                tmem_st16(ta, h);
             } else {
               const uint32_t arow = stage + m * kATile + (i >> 3) * 1024 + (i & 7) * 128;
 #pragma unroll
