@@ -56,6 +56,7 @@ EXPERT_BYTES = 3 * PROJ_BYTES          # 99,090,624 B of NF4 weights per expert
 METRIC = "Mixtral NF4 decode tok/s (bs1, bs64); expert GEMV HBM GB/s vs peak"
 SEED = 1
 PROFILE_TRAFFIC = ROOT / "profiles" / "expert_stage_decode_bs1.md"
+PROFILE_PREFILL = ROOT / "profiles" / "grouped_gemm_prefill.md"
 
 
 # ----------------------------------------------------------------------------
@@ -233,6 +234,14 @@ def _max_over_ranks(x: float, world: int, device) -> float:
 def _barrier(world: int):
     if world > 1:
         torch.distributed.barrier()
+
+
+def _profile_value(path, key: str):
+    """A ``key = number`` line of a committed ncu summary (None if absent)."""
+    if not path.exists():
+        return None
+    m = re.search(key + r"\s*[:=]\s*([0-9.eE+]+)", path.read_text())
+    return float(m.group(1)) if m else None
 
 
 def _profile_traffic():
@@ -559,7 +568,8 @@ def measure_batches(gates, tables, dev, L: int, K: int):
                       "expert_loads_last_layer": loads,
                       "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak[0],
                                    "unit": "TFLOP/s", "frac": round(tflops / peak[0], 4),
-                                   "traffic": None,
+                                   "traffic": _profile_value(PROFILE_PREFILL,
+                                                             "traffic_per_layer_bytes"),
                                    "kernel": "grouped NF4 GEMM (gate_up + down launches), per layer",
                                    "algorithmic_flop_per_launch": flops,
                                    "launch_us": round(ms_st * 1e3, 1), "peak_source": peak[1]}}
