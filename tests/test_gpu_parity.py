@@ -311,3 +311,69 @@ def test_layer_forward_mixtral_bs1():
     assert np.array_equal(idx.cpu().numpy(), ridx)
     r, m = assert_close_fp16(out.cpu().numpy(), ref, what="mixtral layer bs1")
     print(f"mixtral layer bs1: rel_l2={r:.2e} max_abs={m:.2e}")
+
+
+# ---------------------------------------------------------------------------
+# One-token layer in one launch (routing, experts and combine in one kernel)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("E,k,H,I", [
+    (16, 2, 256, 512),    # the largest expert count
+    (5, 1, 256, 512),     # k = 1
+    (8, 8, 256, 512),     # every expert routed
+    (4, 2, 2048, 5632),   # last down split partial (5632 = 2 x 2048 + 1536)
+    (8, 2, 1024, 2048),   # one 64-element block per warp in gate_up
+    (2, 2, 8192, 1024),   # eight blocks per warp; two row vectors per routing thread
+])
+def test_layer_forward_one_token_fused(E, k, H, I):
+    """The fused 1-token layer against the oracle, and its routing against the
+    standalone router kernel (same fp16 logits, softmax and top-k)."""
+    from moeinfra_b200 import _native, kernels
+
+    h, wg, experts = _layer_case(1, H, I, E, k, seed=11 * E + k + H // 256)
+    gx = [gpu_expert(ex, H, I) for ex in experts]
+    table = kernels.expert_array([g.nf4_descriptor for g in gx])
+    out, idx, w = kernels.layer_forward(_t(h), _t(wg), table, k, H, I)
+    ref, ridx, rw, _ = omoe.moe_layer_forward(h, wg, experts, H, I, k)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    _, rw_k, ridx_k = kernels.router_topk(_t(h), _t(wg), k, with_logits=False)
+    assert torch.equal(idx, ridx_k)
+    np.testing.assert_allclose(w.cpu().numpy(), rw_k.cpu().numpy(), rtol=1e-6, atol=0)
+    assert_close_fp16(out.cpu().numpy(), ref, what=f"fused 1-token layer E={E} k={k} {H}x{I}")
+    assert _native.take_device_error() == 0
+
+
+def test_layer_forward_one_token_repeated_calls():
+    """Back-to-back calls reuse the wrapper's workspace (its counters are
+    zeroed by the layer itself each call); every result matches the oracle."""
+    from moeinfra_b200 import _native, kernels
+
+    H, I, E, k = 256, 512, 8, 2
+    _, wg, experts = _layer_case(1, H, I, E, k, seed=91)
+    gx = [gpu_expert(ex, H, I) for ex in experts]
+    table = kernels.expert_array([g.nf4_descriptor for g in gx])
+    rng = np.random.default_rng(92)
+    for call in range(3):
+        h = rng.standard_normal((1, H), dtype=np.float32).astype(np.float16)
+        out, _, _ = kernels.layer_forward(_t(h), _t(wg), table, k, H, I, routing=False)
+        ref, _, _, _ = omoe.moe_layer_forward(h, wg, experts, H, I, k)
+        assert_close_fp16(out.cpu().numpy(), ref, what=f"repeated 1-token call {call}")
+    assert _native.take_device_error() == 0
+
+
+def test_layer_forward_gemm_narrow_multitile():
+    """Narrow grouped-GEMM tiles (<= 64 tokens per expert on average) with one
+    expert past 64 tokens, so it spans two token tiles."""
+    from moeinfra_b200 import _native, kernels
+
+    T, H, I, E, k = 120, 256, 512, 2, 1
+    h, wg, experts = _layer_case(T, H, I, E, k, seed=127, gate_std=0.3)
+    _, _, ridx0 = orouter.route_with_logits(h, wg, k)
+    assert np.bincount(ridx0.reshape(-1), minlength=E).max() > 64
+    gx = [gpu_expert(ex, H, I) for ex in experts]
+    table = kernels.expert_array([g.nf4_descriptor for g in gx])
+    out, idx, w = kernels.layer_forward(_t(h), _t(wg), table, k, H, I)
+    ref, ridx, rw, _ = omoe.moe_layer_forward(h, wg, experts, H, I, k)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    assert_close_fp16(out.cpu().numpy(), ref, what="narrow multi-tile layer")
+    assert _native.take_device_error() == 0
