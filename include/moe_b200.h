@@ -157,6 +157,12 @@ int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t* x,
  *   h fp16 [T, hidden], wg fp16 [E, hidden], experts[E] (host array)
  *   out fp16 [T, hidden]; indices int64 [T, k] and weights fp32 [T, k]
  *   receive the routing (both required).
+ * The workspace needs no initialisation (the layer zeroes the counters it
+ * keeps there); calls sharing a workspace must be ordered on the device.
+ * T == 1 runs as two launches: the counters, then one kernel that routes,
+ * runs both projections and combines.  That kernel's CTAs (one per SM) wait
+ * on one another's progress, so it needs the whole GPU's SMs; every such wait
+ * is bounded, and a timeout sets the word read by moe_take_device_error.
  */
 size_t moe_layer_workspace_size(int64_t T, int hidden, int inter, int E, int k);
 int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
