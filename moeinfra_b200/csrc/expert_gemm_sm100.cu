@@ -7,22 +7,26 @@
 // fp16 GEMM with fp32 accumulation:  w = fp16(bf16(code * absmax)).
 //
 // One launch per projection; a persistent CTA per SM walks tiles of
-// (expert, 128 weight rows, up to 256 tokens of that expert):
-//   gate_up: D1 = W1 . X^T and D3 = W3 . X^T in TMEM (2 x 256 fp32 columns),
+// (expert, 128 weight rows, up to kTileN tokens of that expert):
+//   gate_up: D1 = W1 . X^T and D3 = W3 . X^T in TMEM (2 x kTileN fp32 columns),
 //            epilogue h = fp16(silu(fp16(D1)) * fp16(D3)) -> h_sorted [P, I];
-//   down   : D = W2 . H^T (256 columns), epilogue y = fp16(D) -> y_sorted [P, H].
-// Warp roles (320 threads):
-//   warps 0-7  dequantize the 128 x 64 weight tile of each K step (one NF4
-//              block per row; warp w takes rows 32*(w%4).., byte part w/4)
-//              straight into shared memory in the UMMA K-major 128-byte
-//              swizzled layout, then run the epilogue (TMEM -> registers ->
-//              global);
-//   warp 8     lane 0 loads the token tile of each K step with TMA (no
+//   down   : D = W2 . H^T (kTileN columns), epilogue y = fp16(D) -> y_sorted [P, H].
+// Two configurations: wide (prefill: 256-token tiles, 8 dequant warps) and
+// narrow (decode batches of at most ~64 tokens per expert: 64-token tiles, 16
+// dequant warps).  Warp roles (DQ dequant warps + 2):
+//   warps 0..DQ-1  dequantize the 128 x 64 weight tile of each K step (one
+//              NF4 block per row; warp w takes rows 32*(w%4).., byte part w/4)
+//              either into shared memory in the UMMA K-major 128-byte swizzled
+//              layout (wide gate_up) or into tensor memory with tcgen05.st
+//              (narrow tiles, wide down), then run the epilogue (TMEM ->
+//              registers -> global);
+//   warp DQ    lane 0 loads the token tile of each K step with TMA (no
 //              multicast; rows past the tensor read as zeros);
-//   warp 9     lane 0 issues tcgen05.mma (kind::f16, M = 128, N = tokens
-//              rounded up to 16, K = 16 per instruction) and commits stages.
-// Stage barriers: a_full (8 dequant warps), b_full (TMA bytes), empty (MMA
-// commit); accumulator barriers acc_full (MMA commit) and acc_empty (8
+//   warp DQ+1  lane 0 issues tcgen05.mma (kind::f16, M = 128, N = tokens
+//              rounded up to 16, K = 16 per instruction; A from shared or
+//              tensor memory) and commits stages.
+// Stage barriers: a_full (DQ dequant warps), b_full (TMA bytes), empty (MMA
+// commit); accumulator barriers acc_full (MMA commit) and acc_empty (DQ
 // epilogue warps).  Every wait is bounded: on timeout the GEMM error word is
 // set, the waiting role stops, and before exit the CTA waits (bounded) for its
 // issued copies and MMAs, then frees its TMEM.
@@ -46,7 +50,6 @@ template <int DQ>
 constexpr int threads_for() { return (DQ + 2) * 32; }
 constexpr uint32_t kATile = kBM * kBK * 2;         // 16 KB fp16, swizzled
 constexpr uint32_t kBBox = kBoxRows * kBK * 2;      // 8 KB
-constexpr uint32_t kBTile = kMaxN * kBK * 2;        // 32 KB
 constexpr uint32_t kLutBytes = 256 * 16 * 8;        // byte -> (code hi, code lo), 16 replicas
 // Narrow tiles: the table (32 replicas, 64 KB) sits at shared-window address
 // 0x10000, entry (byte v, lane l) at 0x10000 | v << 8 | l * 8, so one byte
