@@ -29,8 +29,14 @@
 //     order (deterministic).
 //   gate_up: item = 8 rows; MMA rows 0..7 are W1 rows, 8..15 the same W3 rows,
 //            so g and u of a (row, token) end up in one thread.
-//   down   : item = (16 rows, K split s of 2048 elements); split partials go
-//            to y_part[slot][S][H] and the combine kernel sums them in order.
+//   down   : item = (16 rows per tile, 2 tiles for 1-token experts; K split s
+//            of 2048 elements); split partials go to y_part[slot][S][H] and
+//            are summed in split order by the combine.
+// Both phases run in one launch per layer and token kind (k_stage_mma): a
+// CTA's down items wait (bounded) on per-split counters that the CTAs
+// producing those h rows publish.  For a 1-token layer the same launch also
+// routes the token (in every CTA) and the last CTA to finish each 32-row
+// group of the output writes its weighted combine.
 #include "common.cuh"
 #include "router_device.cuh"
 
