@@ -35,7 +35,8 @@ typedef enum moe_status {
   MOE_ERR_CUDA = 3,
   MOE_ERR_WORKSPACE = 4,
   MOE_ERR_ALIGNMENT = 5,
-  MOE_ERR_TIMEOUT = 6
+  MOE_ERR_TIMEOUT = 6,
+  MOE_ERR_CODEBOOK = 7
 } moe_status_t;
 
 #define MOE_MAX_EXPERTS 16
@@ -68,10 +69,40 @@ const char* moe_version(void);
  * count taken around a capture is the kernel count of one replay. */
 uint64_t moe_launch_count(void);
 
-/* Reads and clears the device-side error word that kernels set when one of
- * their bounded waits (bulk-copy pipeline barriers) times out.  Synchronous
- * (a device-to-host copy).  *value is 0 when no wait timed out. */
+/* Reads and clears the device-side error words of the current device.
+ * Kernels never trap; they record a problem found on the device as bits:
+ *   1  a bounded wait (cross-CTA counter, mbarrier phase) ran out; the
+ *      launch's outputs are invalid;
+ *   2  the experts of one launch carry different NF4 codebooks (the kernels
+ *      decode every expert with expert 0's w1 codebook for gate/up and its
+ *      w2 codebook for down); the outputs are invalid;
+ *   4  a kernel found its shared-memory layout not as planned and skipped.
+ * Synchronous (device-to-host copies).  *value is 0 when nothing was set. */
 int moe_take_device_error(int* value);
+
+/* Synchronises `stream`, then turns the device error words into a status:
+ * MOE_ERR_TIMEOUT (bit 1), MOE_ERR_CODEBOOK (bit 2), MOE_ERR_CUDA (bit 4 or a
+ * CUDA error), else MOE_OK.  The words are cleared.  Call it at the points
+ * where the caller synchronises anyway (end of a step, before reading
+ * results back) to learn whether the launches since the last check were valid.
+ * No counterpart in the reference (its library calls raise synchronously). */
+int moe_stream_check(void* stream);
+
+/* Limit of every bounded device wait, in nanoseconds of the GPU's global
+ * timer (default 2 s; accepted range 1 us .. 60 s).  Launches read it when
+ * they are enqueued (a captured CUDA graph keeps the value it was captured
+ * with).  After the limit a wait gives up, sets error bit 1 and lets the
+ * kernel run to its end, so a GPU is never held by a wait that cannot end. */
+int moe_set_wait_limit_ns(uint64_t ns);
+uint64_t moe_wait_limit_ns(void);
+
+/* One bounded wait, on one thread, until the int at `flag` (device memory)
+ * reaches `target`: the same acquire-poll-with-limit the layer kernels use
+ * between CTAs.  A health check of the timeout path: with a flag nothing
+ * sets, it gives up after moe_wait_limit_ns() and moe_stream_check() returns
+ * MOE_ERR_TIMEOUT.  waited_ns (device int, may be NULL) receives the time
+ * spent waiting. */
+int moe_probe_wait(const int* flag, int target, int* waited_ns, void* stream);
 
 /* ---------------------------------------------------------------------------
  * NF4 blockwise dequant to bf16, bit-exact:
@@ -149,6 +180,15 @@ int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t* x,
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Codebooks.  moe_expert_forward, moe_experts_forward, moe_layer_forward and
+ * moe_layer_forward_noalloc decode every expert of one call with expert 0's
+ * codebooks (w1's for w1 and w3, w2's for w2).  All experts of one call must
+ * carry equal codebook values (every NF4 store made by the reference's
+ * quantizer does: the standard NF4 table).  A call whose experts differ is
+ * detected on the device: its outputs are invalid and moe_stream_check()
+ * returns MOE_ERR_CODEBOOK.
+ *
+ * ---------------------------------------------------------------------------
  * One sparse-MoE layer: router -> permute -> experts -> weighted combine,
  * with no host synchronisation.  Replaces MoELayer._forward_tokens
  * (model/moe_layer.py:117-211) for GPU-resident experts: routing
@@ -186,10 +226,14 @@ int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
  * moe_layer_workspace_size() exceeds it returns MOE_ERR_WORKSPACE and does
  * nothing.  The array's address is looked up (cudaGetSymbolAddress) on the
  * first call on each device and cached; make that first call before any
- * stream capture on the device.  Calls that overlap on one device (other
- * streams or host threads without ordering) race on the one array: serialise
- * them.  Nothing in the array needs to start at zero.  Same results as
- * moe_layer_forward.
+ * stream capture on the device.  The scratch used is the CURRENT device's
+ * (cudaGetDevice), which must be the device `stream` belongs to; the cached
+ * address is invalid after cudaDeviceReset on that device.  Calls that overlap
+ * on one device (other streams or host threads without ordering) race on the
+ * one array: serialise them.  Nothing in the array needs to start at zero.
+ * Same results as moe_layer_forward; like it, a wait that timed out or a
+ * codebook mismatch is only visible through moe_stream_check() /
+ * moe_take_device_error(), which callers must poll at their sync points.
  */
 #define MOE_NOALLOC_SCRATCH_BYTES ((size_t)4 << 20)
 int moe_layer_forward_noalloc(const uint16_t* h, const uint16_t* wg,

@@ -14,6 +14,8 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmoe_b200.so"
 
 MOE_MAX_EXPERTS = 16
+MOE_ERR_TIMEOUT = 6
+MOE_ERR_CODEBOOK = 7
 MOE_NOALLOC_SCRATCH_BYTES = 4 << 20
 
 
@@ -31,6 +33,10 @@ SIGNATURES: dict[str, tuple] = {
     "moe_version": (ctypes.c_char_p, []),
     "moe_launch_count": (ctypes.c_uint64, []),
     "moe_take_device_error": (c_int, [ctypes.POINTER(c_int)]),
+    "moe_stream_check": (c_int, [c_void_p]),
+    "moe_set_wait_limit_ns": (c_int, [ctypes.c_uint64]),
+    "moe_wait_limit_ns": (ctypes.c_uint64, []),
+    "moe_probe_wait": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     "moe_nf4_dequant": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "moe_nf4_tile16": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "moe_nf4_dequant_tile16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
@@ -101,10 +107,25 @@ def launch_count() -> int:
 
 
 def take_device_error() -> int:
-    """Read and clear the device error word (1 = a bounded kernel wait timed out)."""
+    """Read and clear the device error words (bit 1: a bounded kernel wait timed
+    out; bit 2: experts of one launch carried different codebooks)."""
     v = c_int(0)
     check(lib().moe_take_device_error(ctypes.byref(v)), "moe_take_device_error")
     return v.value
+
+
+def stream_check(stream: int | None) -> int:
+    """Synchronise ``stream`` and return the status of the launches since the last check."""
+    return int(lib().moe_stream_check(c_void_p(stream)))
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Limit of every bounded device wait (nanoseconds of the GPU's global timer)."""
+    check(lib().moe_set_wait_limit_ns(int(ns)), "moe_set_wait_limit_ns")
+
+
+def wait_limit_ns() -> int:
+    return int(lib().moe_wait_limit_ns())
 
 
 def check(status: int, what: str) -> None:

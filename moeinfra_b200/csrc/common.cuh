@@ -60,15 +60,62 @@ __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + 
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-inline int sm_count() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+// Host-side state kept per CUDA device (the current device of the calling
+// thread): SM count, one-time kernel attribute setup.  A process may drive
+// several GPUs, so none of it is a process-wide single value.
+constexpr int kMaxDevices = 64;
+int current_device();  // cudaGetDevice(), or -1 on error / out of range
+int sm_count();        // SMs of the current device (148 if it cannot be queried)
+// Runs setup() once per (key, device) and remembers whether it succeeded.
+bool once_per_device(const void* key, bool (*setup)());
+
+// Bounded device waits.  Every spin (cross-CTA counters, mbarrier phases)
+// gives up after the limit in nanoseconds of %globaltimer, sets a bit of the
+// device error word and lets the kernel finish; the limit rides in each
+// kernel's arguments (moe_set_wait_limit_ns) so a graph replays the value
+// captured with it.
+uint64_t wait_limit_ns();
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Device error word bits (read and cleared by moe_take_device_error).
+constexpr int kErrWaitTimeout = 1;    // a bounded wait ran out
+constexpr int kErrCodebook = 2;       // experts of one launch carry different codebooks
+constexpr int kErrSmemLayout = 4;     // shared-memory layout not as planned (launch skipped)
+
+// Each translation unit whose kernels report errors owns one device word
+// (device code is compiled per file, without relocatable linking, so a word
+// cannot be shared across files); its host-side reader registers itself with
+// moe_take_device_error, which ORs every word and clears it.
+void register_error_reader(int (*reader)(int*));
+#define MOE_DEFINE_ERROR_WORD()                                                          \
+  namespace {                                                                            \
+  __device__ int g_device_error = 0;                                                     \
+  __device__ __forceinline__ void set_device_error(int bits) {                          \
+    atomicOr(&g_device_error, bits);                                                     \
+  }                                                                                      \
+  int read_clear_error(int* value) {                                                     \
+    int v = 0;                                                                           \
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return 1; \
+    if (v != 0) {                                                                        \
+      const int zero = 0;                                                                \
+      if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess) return 1; \
+    }                                                                                    \
+    *value = v;                                                                          \
+    return 0;                                                                            \
+  }                                                                                      \
+  const bool g_error_reader_registered = (register_error_reader(&read_clear_error), true); \
   }
-  return n;
+
+// True when the 16 fp32 codebook entries at a and b are equal.
+__device__ __forceinline__ bool same_code16(const float* a, const float* b) {
+  if (a == b) return true;
+  bool same = true;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) same &= __ldg(a + i) == __ldg(b + i);
+  return same;
 }
 
 // fp16 <-> float on raw bit patterns.

@@ -68,6 +68,7 @@ struct DecodeArgs {
   int64_t* out_indices;      // [k] routed experts (written by CTA 0)
   uint16_t* out;             // [H] fp16 layer output
   int* rg_count;             // [H / 16] row-group completion counters, zeroed
+  uint64_t wait_ns;          // limit of every bounded wait (moe_set_wait_limit_ns)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -380,9 +381,7 @@ struct Cursor {
 // before it reads the split's h rows, which it reads through L2 (ld.cg).
 // The counters are zeroed by the kernel that runs before each launch on the
 // stream (permute / offsets) or by a memset.
-constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
-
-__device__ int g_decode_error = 0;
+MOE_DEFINE_ERROR_WORD()
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
@@ -390,14 +389,15 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   return v;
 }
 
-// Bounded wait until *p >= target; on timeout records the error and returns
-// (the launch's results are then invalid, the host reads the error word).
-__device__ __forceinline__ void wait_count(const int* p, int target) {
+// Bounded wait until *p >= target; after limit_ns of %globaltimer it records
+// the timeout in the device error word and returns (the launch's results are
+// then invalid; moe_stream_check reports MOE_ERR_TIMEOUT).
+__device__ __forceinline__ void wait_count(const int* p, int target, uint64_t limit_ns) {
   if (ld_acquire(p) >= target) return;
-  const long long t0 = clock64();
+  const uint64_t t0 = globaltimer_ns();
   while (ld_acquire(p) < target) {
-    if (clock64() - t0 > kWaitCycles) {
-      atomicOr(&g_decode_error, 1);
+    if (globaltimer_ns() - t0 > limit_ns) {
+      set_device_error(kErrWaitTimeout);
       return;
     }
     __nanosleep(256);
@@ -689,7 +689,7 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
       tok0 = s_off[e];
       n = s_off[e + 1] - tok0;
       // h rows of this split come from other CTAs' gate_up items.
-      wait_count(a.sync + c_ai * a.S + c_s, split_items(I, c_s));
+      wait_count(a.sync + c_ai * a.S + c_s, split_items(I, c_s), a.wait_ns);
       const int blk0 = c_s * kSplitBlocks + wblk;
       const int tok = kMulti ? g : 0;
       const bool valid = tok < n;
@@ -921,12 +921,20 @@ __device__ __forceinline__ void combine_rows(const DecodeArgs& a, const Active& 
   }
 }
 
-__device__ __forceinline__ bool same_codebook(const float* a, const float* b) {
-  if (a == b) return true;
-  bool same = true;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) same &= __ldg(a + i) == __ldg(b + i);
-  return same;
+// The decode tables come from expert 0's codebooks (w1 for gate_up, w2 for
+// down); CTA 0 checks that every active expert carries the same ones and
+// flags the launch otherwise (moe_stream_check: MOE_ERR_CODEBOOK).
+__device__ __forceinline__ void check_codebooks(const DecodeArgs& a, const Active& act,
+                                                const int* s_active) {
+  if (blockIdx.x != 0) return;
+  const int i = threadIdx.x;
+  if (i < act.n * 3) {
+    const moe_nf4_expert_t& ex = a.ex.e[s_active[i / 3]];
+    const int m = i % 3;
+    const float* c = m == 0 ? ex.w1.code : m == 1 ? ex.w3.code : ex.w2.code;
+    const float* ref = m == 2 ? a.ex.e[0].w2.code : a.ex.e[0].w1.code;
+    if (!same_code16(c, ref)) set_device_error(kErrCodebook);
+  }
 }
 
 // One launch per layer for the experts of one kind (1 token or 2..8 tokens):
@@ -956,12 +964,13 @@ __global__ void __launch_bounds__(kThreadsK, 1) k_stage_mma(const __grid_constan
   const Active act = routed ? route_token(a, wpre, s_off, s_active, s_route)
                             : load_active<kMulti>(a, s_off, s_active);
   if (act.n == 0) return;
+  check_codebooks(a, act, s_active);
   if (kMulti) lut_ok = room && build_lut(a.ex.e[0].w1.code, smem);
   if (!lut_ok) return;
   const StageSmem sm{reinterpret_cast<float*>(smem), s_off, s_active, s_meta,
                      routed ? s_route.zero_tok : a.pair_token};
   gate_phase<NBW, kMulti, kFullG>(a, act, sm);
-  if (!same_codebook(a.ex.e[0].w1.code, a.ex.e[0].w2.code)) {
+  if (!same_code16(a.ex.e[0].w1.code, a.ex.e[0].w2.code)) {
     __syncthreads();
     build_lut(a.ex.e[0].w2.code, smem);
   }
@@ -1021,6 +1030,7 @@ bool attrs() {
   return attrs_nbw<1, kMulti>() && attrs_nbw<2, kMulti>() && attrs_nbw<4, kMulti>() &&
          attrs_nbw<8, kMulti>();
 }
+bool decode_attrs() { return attrs<false>() && attrs<true>(); }
 
 // Blocks per K part of the gate_up phase: ceil(H / 64 / 16) rounded up to a
 // power of two (parts past the row are idle).
@@ -1081,8 +1091,8 @@ int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t*
                           int max_tokens_per_expert, cudaStream_t s) {
   if (E < 1 || E > MOE_MAX_EXPERTS || !sync) return MOE_ERR_INVALID_ARG;
   if (!decode_supported(hidden, inter)) return MOE_ERR_UNSUPPORTED;
-  static bool attr_ok = attrs<false>() && attrs<true>();
-  if (!attr_ok) return MOE_ERR_CUDA;
+  if (!once_per_device(reinterpret_cast<const void*>(&decode_attrs), &decode_attrs))
+    return MOE_ERR_CUDA;
   DecodeArgs a{};
   for (int e = 0; e < E; ++e) a.ex.e[e] = experts[e];
   a.E = E;
@@ -1095,6 +1105,7 @@ int launch_decode_experts(const moe_nf4_expert_t* experts, int E, const int32_t*
   a.I = inter;
   a.S = decode_splits(inter);
   a.sync = sync;
+  a.wait_ns = wait_limit_ns();
   int st = launch_stage<false>(a, s);
   if (st == MOE_OK && max_tokens_per_expert > 1) {
     a.sync = sync + MOE_MAX_EXPERTS * a.S;
@@ -1113,8 +1124,8 @@ int launch_decode_layer1(const moe_nf4_expert_t* experts, int E, int k, const ui
       !rg_count)
     return MOE_ERR_INVALID_ARG;
   if (!decode_supported(hidden, inter)) return MOE_ERR_UNSUPPORTED;
-  static bool attr_ok = attrs<false>() && attrs<true>();
-  if (!attr_ok) return MOE_ERR_CUDA;
+  if (!once_per_device(reinterpret_cast<const void*>(&decode_attrs), &decode_attrs))
+    return MOE_ERR_CUDA;
   DecodeArgs a{};
   for (int e = 0; e < E; ++e) a.ex.e[e] = experts[e];
   a.E = E;
@@ -1131,17 +1142,8 @@ int launch_decode_layer1(const moe_nf4_expert_t* experts, int E, int k, const ui
   a.out_indices = indices;
   a.out = out;
   a.rg_count = rg_count;
+  a.wait_ns = wait_limit_ns();
   return launch_stage<false>(a, s);
-}
-
-// Reads and clears the decode error word (a bounded cross-CTA wait timed out).
-int decode_take_error(int* value) {
-  int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_decode_error, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
-  const int zero = 0;
-  if (cudaMemcpyToSymbol(g_decode_error, &zero, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
-  *value = v;
-  return MOE_OK;
 }
 
 int launch_reduce_partials(const float* part, int64_t P, int S, int width, uint16_t* y,

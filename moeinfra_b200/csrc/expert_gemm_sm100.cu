@@ -55,9 +55,7 @@ constexpr uint32_t kLutBytes = 256 * 16 * 8;        // byte -> (code hi, code lo
 // 0x10000, entry (byte v, lane l) at 0x10000 | v << 8 | l * 8, so one byte
 // permute of the packed word forms the address.
 constexpr uint32_t kLutWin = 0x10000;
-constexpr long long kWaitCycles = 4000000000LL;     // ~2 s at 2 GHz
-
-__device__ int g_gemm_error = 0;
+MOE_DEFINE_ERROR_WORD()
 
 // kNarrow: tiles of at most 64 tokens (one TMA box), whose token slot is a
 // quarter of the wide one, so more stages fit and hide the per-stage hand-off.
@@ -97,6 +95,7 @@ struct GemmArgs {
   int K;                   // reduction length (H for gate_up, I for down)
   int rows;                // output rows per expert (I for gate_up, H for down)
   uint16_t* out;           // [P, rows] fp16
+  uint64_t wait_ns;        // limit of every bounded wait (moe_set_wait_limit_ns)
 };
 
 // ---- PTX wrappers ----------------------------------------------------------
@@ -120,13 +119,14 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase of `parity`; false (error word set) after ~kWaitCycles.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Waits for the phase of `parity`; false (error word set) after limit_ns of
+// %globaltimer.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try(bar, parity)) return true;
-  const long long t0 = clock64();
+  const uint64_t t0 = globaltimer_ns();
   while (!mbar_try(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) {
-      atomicExch(&g_gemm_error, 1);
+    if (globaltimer_ns() - t0 > limit_ns) {
+      set_device_error(kErrWaitTimeout);
       return false;
     }
   }
@@ -134,9 +134,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 }
 // Warp-uniform wait: lane 0 waits, the result is broadcast (all lanes of a
 // warp then take the same path through warp-collective tcgen05 instructions).
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, limit_ns) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   __syncwarp();
   return ok != 0;
@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
   const int mtiles = a.rows / kBM;
   const int nblk = a.K / kBK;
   if (C::kLutWindow && (base + NS * C::kStage > kLutWin || raw + C::kSmem < 2 * kLutWin)) {
-    if (threadIdx.x == 0) atomicExch(&g_gemm_error, 1);  // shared-memory layout not as planned
+    if (threadIdx.x == 0) set_device_error(kErrSmemLayout);  // shared-memory layout not as planned
     return;
   }
 
@@ -367,6 +367,15 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
       asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(lut + i * 8), "f"(c.x), "f"(c.y)
                    : "memory");
     }
+  }
+  // The decode table comes from expert 0's codebook; CTA 0 flags a launch whose
+  // experts with tokens carry another one (moe_stream_check: MOE_ERR_CODEBOOK).
+  if (blockIdx.x == 0 && threadIdx.x < a.E * C::kMats && s_off[threadIdx.x / C::kMats + 1] >
+                                                           s_off[threadIdx.x / C::kMats]) {
+    const moe_nf4_expert_t& ex = a.ex.e[threadIdx.x / C::kMats];
+    const float* c = kGate ? ((threadIdx.x % C::kMats) ? ex.w3.code : ex.w1.code) : ex.w2.code;
+    if (!same_code16(c, kGate ? a.ex.e[0].w1.code : a.ex.e[0].w2.code))
+      set_device_error(kErrCodebook);
   }
   tc_fence_before();
   __syncthreads();
@@ -425,7 +434,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
           if (kb >= nblk) break;
           const int s = g % NS;
           stop = __shfl_sync(0xffffffffu, s_abort, 0) != 0 ||
-                 !warp_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1);
+                 !warp_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1, a.wait_ns);
           if (stop) {
             s_abort = 1;
             break;
@@ -487,7 +496,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
       if (stop) break;
       // Epilogue: this warp reads TMEM lanes 32*rw.. ; column chunks of 16,
       // alternating between the two byte halves' warps.
-      if (!warp_wait(saddr(&s_accfull), it & 1)) {
+      if (!warp_wait(saddr(&s_accfull), it & 1, a.wait_ns)) {
         s_abort = 1;
         break;
       }
@@ -528,7 +537,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
         const int row0 = s_off[tl.e] + tl.n0;
         for (int kb = 0; kb < nblk; ++kb, ++g) {
           const int s = g % NS;
-          if (!s_abort && !mbar_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1)) s_abort = 1;
+          if (!s_abort && !mbar_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1, a.wait_ns)) s_abort = 1;
           if (s_abort) break;
           const uint32_t bar = saddr(&s_bfull[s]);
           const uint32_t bt = base + s * C::kStage + C::kAStage;
@@ -540,7 +549,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
       // Copies issued into stages never consumed (timeout): let them land.
       if (s_abort)
         for (uint32_t j = g > (uint32_t)NS ? g - NS : 0; j < g; ++j)
-          mbar_wait(saddr(&s_bfull[j % NS]), (j / NS) & 1);
+          mbar_wait(saddr(&s_bfull[j % NS]), (j / NS) & 1, a.wait_ns);
     }
   } else {
     // ---------------- MMA issuer ----------------
@@ -551,15 +560,15 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
         const Tile tl = tile_of<C::kTileN>(t, s_base, s_off, a.E, mtiles);
         const int n = (tl.nt + 15) & ~15;
         const uint32_t idesc = instr_desc(n);
-        if (!mbar_wait(saddr(&s_accempty), (it & 1) ^ 1)) {
+        if (!mbar_wait(saddr(&s_accempty), (it & 1) ^ 1, a.wait_ns)) {
           s_abort = 1;
           break;
         }
         tc_fence_after();
         for (int kb = 0; kb < nblk; ++kb, ++g) {
           const int s = g % NS;
-          if (!mbar_wait(saddr(&s_afull[s]), (g / NS) & 1) ||
-              !mbar_wait(saddr(&s_bfull[s]), (g / NS) & 1)) {
+          if (!mbar_wait(saddr(&s_afull[s]), (g / NS) & 1, a.wait_ns) ||
+              !mbar_wait(saddr(&s_bfull[s]), (g / NS) & 1, a.wait_ns)) {
             s_abort = 1;
             break;
           }
@@ -587,7 +596,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
       // After a timeout, wait (bounded) for the MMAs already issued.
       if (s_abort && issued_any) {
         tc_commit(saddr(&s_drain));
-        mbar_wait(saddr(&s_drain), 0);
+        mbar_wait(saddr(&s_drain), 0, a.wait_ns);
       }
     }
   }
@@ -633,11 +642,16 @@ bool make_token_map(CUtensorMap* map, const uint16_t* x, int64_t rows_total, int
 }
 
 template <bool kGate, int DQ>
+bool gemm_attr() {
+  return cudaFuncSetAttribute(k_grouped_gemm<kGate, DQ>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              Cfg<kGate, DQ == 16>::kSmem) == cudaSuccess;
+}
+
+template <bool kGate, int DQ>
 int launch_dq(const GemmArgs& a, const CUtensorMap& map, cudaStream_t s) {
-  static bool attr = cudaFuncSetAttribute(k_grouped_gemm<kGate, DQ>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          Cfg<kGate, DQ == 16>::kSmem) == cudaSuccess;
-  if (!attr) return MOE_ERR_CUDA;
+  if (!once_per_device(reinterpret_cast<const void*>(&gemm_attr<kGate, DQ>), &gemm_attr<kGate, DQ>))
+    return MOE_ERR_CUDA;
   k_grouped_gemm<kGate, DQ><<<sm_count(), threads_for<DQ>(), Cfg<kGate, DQ == 16>::kSmem, s>>>(a, map);
   MOE_CHECK_LAUNCH();
   return MOE_OK;
@@ -682,22 +696,13 @@ int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
   a.K = hidden;
   a.rows = inter;
   a.out = h_sorted;
+  a.wait_ns = wait_limit_ns();
   int st = launch_one<true>(a, x_sorted, P, s);
   if (st != MOE_OK) return st;
   a.K = inter;
   a.rows = hidden;
   a.out = y_sorted;
   return launch_one<false>(a, h_sorted, P, s);
-}
-
-// Reads and clears the GEMM error word (a bounded barrier wait timed out).
-int gemm_take_error(int* value) {
-  int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
-  const int zero = 0;
-  if (cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int)) != cudaSuccess) return MOE_ERR_CUDA;
-  *value = v;
-  return MOE_OK;
 }
 
 }  // namespace moe

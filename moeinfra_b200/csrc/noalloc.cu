@@ -15,11 +15,11 @@
 #include "common.cuh"
 
 namespace moe {
+bool decode_supported(int hidden, int inter);  // expert_decode.cu
+
 namespace {
 
 constexpr size_t kNoAllocScratch = MOE_NOALLOC_SCRATCH_BYTES;
-constexpr int kMaxDevices = 64;
-
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch];
 
 std::mutex g_scratch_mu;
@@ -47,7 +47,11 @@ extern "C" int moe_layer_forward_noalloc(const uint16_t* h, const uint16_t* wg,
                                          int hidden, int inter, uint16_t* out, int64_t* indices,
                                          float* weights, void* stream) {
   using namespace moe;
-  if (T < 0 || E < 1 || k < 1) return MOE_ERR_INVALID_ARG;
+  // The same argument checks as moe_layer_forward, before the size check, so
+  // a bad call reports what is wrong with it rather than a size.
+  if (T < 0 || E < 1 || E > MOE_MAX_EXPERTS || k < 1 || k > E || k > 8) return MOE_ERR_INVALID_ARG;
+  if (!decode_supported(hidden, inter)) return MOE_ERR_UNSUPPORTED;
+  if (T == 0) return MOE_OK;
   const size_t need = moe_layer_workspace_size(T, hidden, inter, E, k);
   if (need > kNoAllocScratch) return MOE_ERR_WORKSPACE;
   void* scratch = nullptr;

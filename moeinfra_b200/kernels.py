@@ -55,6 +55,32 @@ def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
 
 
+def check_device(device: torch.device | int | None = None) -> None:
+    """Synchronise the current stream of ``device`` and raise if a kernel flagged an error.
+
+    Kernels never trap: a bounded wait that ran out, or experts of one launch
+    with different codebooks, leave a bit in the device error word and the
+    launch's outputs invalid.  Call this where the caller synchronises anyway
+    (the end of a step, before reading results back).
+    """
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index))
+    with torch.cuda.device(dev):
+        status = _native.stream_check(torch.cuda.current_stream(dev).cuda_stream)
+    if status != 0:
+        raise RuntimeError(f"device check failed: {_native.status_string(status)} (status {status})")
+
+
+def probe_wait(flag: torch.Tensor, target: int = 1) -> torch.Tensor:
+    """One bounded device wait until ``flag[0] >= target``; returns the device-side wait time (ns)."""
+    dev = _need_cuda("probe_wait", flag=flag)
+    _need_dtype("probe_wait", flag, torch.int32, "flag")
+    waited = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(_native.lib().moe_probe_wait(_p(flag), int(target), _p(waited), _stream(dev)),
+          "moe_probe_wait")
+    return waited
+
+
 # ---------------------------------------------------------------------------
 # NF4 dequant
 # ---------------------------------------------------------------------------
@@ -235,10 +261,26 @@ def layer_forward_noalloc(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hi
         out = torch.empty(T, hidden, dtype=torch.float16, device=dev)
     idx = torch.empty(T, k, dtype=torch.int64, device=dev)
     w = torch.empty(T, k, dtype=torch.float32, device=dev)
-    check(_native.lib().moe_layer_forward_noalloc(_p(h), _p(wg), experts, len(experts), k, T,
-                                                  hidden, inter, _p(out), _p(idx), _p(w),
-                                                  _stream(dev)), "moe_layer_forward_noalloc")
+    # The library takes the scratch of the CURRENT device: make it h's.
+    with torch.cuda.device(dev):
+        check(_native.lib().moe_layer_forward_noalloc(_p(h), _p(wg), experts, len(experts), k, T,
+                                                      hidden, inter, _p(out), _p(idx), _p(w),
+                                                      _stream(dev)), "moe_layer_forward_noalloc")
     return out, idx, w
+
+
+def routed_layer_forward(h: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor, experts,
+                         hidden: int, inter: int) -> torch.Tensor:
+    """The MoE layer on routing the caller already has (indices int64 / weights fp32 [T, k]).
+
+    permute -> gather -> experts -> ordered fp16 combine, with no second
+    routing pass; every expert slot without tokens in ``indices`` is never read.
+    """
+    E = len(experts)
+    offsets, pair_token, _, pair_slot = permute(indices.contiguous(), weights.contiguous(), E)
+    x_sorted = gather_rows(h.contiguous(), pair_token)
+    y_sorted = experts_forward(experts, offsets, x_sorted, hidden, inter)
+    return combine(y_sorted, pair_slot, indices.contiguous(), weights.contiguous())
 
 
 def experts_forward(experts, expert_offsets: torch.Tensor, x_sorted: torch.Tensor, hidden: int,

@@ -20,11 +20,12 @@ import torch
 from safetensors import safe_open
 
 from moeinfra_b200.model.expert import PrequantizedNF4Expert, QuantizedMixtralExpert
+from moeinfra_b200.model.nf4_format import store_file_name
 from moeinfra_b200.model.types import LayerWeights
 
 
 def expert_filename(layer_id: int, expert_id: int) -> str:
-    return f"layer_{layer_id:02d}_expert_{expert_id:02d}.safetensors"
+    return store_file_name(layer_id, expert_id)
 
 
 class ModelLoader:

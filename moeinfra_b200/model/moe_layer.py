@@ -12,8 +12,9 @@ demoted afterwards.  How it runs on a B200:
 * otherwise (offload mode): route on the GPU, read back the routed set (the
   one device->host sync the residency decision needs, like the reference's
   ``unique().tolist()`` at ``:150-153``), make those experts resident through
-  ``_ensure_expert_on_gpu`` (same seam, ``:39-115``), then the same fused
-  kernels;
+  ``_ensure_expert_on_gpu`` (same seam, ``:39-115``), then permute / experts /
+  combine kernels on that same routing (no second routing pass), and read the
+  device error word at that sync point;
 * experts that are not NF4 GPU experts (e.g. test doubles installed through
   the ``_ensure_expert_on_gpu`` seam) are called one by one on their tokens and
   combined by the same combine kernel.
@@ -152,16 +153,33 @@ class MoELayer:
                 gpu_experts[e] = self._ensure_expert_on_gpu(e)
             table = self._descriptor_array(gpu_experts)
             if table is not None:
+                # The routing computed above is the one used: unrouted expert
+                # slots get zero tokens from these same indices and are never read.
                 inter = next(iter(gpu_experts.values())).intermediate_size
-                return self._fused(hidden_states, table, inter)
-            return self._per_expert(hidden_states, expert_indices, expert_weights, unique_ids,
-                                    gpu_experts)
+                out = kernels.routed_layer_forward(hidden_states.contiguous(), expert_indices,
+                                                   expert_weights, table,
+                                                   self.router.hidden_size, inter)
+            else:
+                out = self._per_expert(hidden_states, expert_indices, expert_weights, unique_ids,
+                                       gpu_experts)
+            # The offload path synchronises anyway (routing read-back, copies):
+            # surface any error a kernel flagged on the device here.
+            kernels.check_device(hidden_states.device)
+            return out
         finally:
             if self.cache_manager is not None:
                 for e in unique_ids:
                     if not was_resident[e]:
                         self.cache_manager.demote_to_cpu(self.layer_id, e)
             gpu_experts.clear()
+
+    def check_device_errors(self) -> None:
+        """Synchronise and raise ``RuntimeError`` if a kernel flagged an error.
+
+        The resident path launches without host synchronisation; callers check
+        at their own sync points (end of a decode step) with this.
+        """
+        kernels.check_device()
 
     def _per_expert(self, h, idx, w, unique_ids, experts) -> torch.Tensor:
         """Generic experts: call each on its tokens, then the ordered fp16 combine kernel."""

@@ -110,6 +110,71 @@ def is_nested(state: dict) -> bool:
     return state.get("state2_absmax") is not None or state.get("state2_code") is not None
 
 
+def check_projection_sizes(state: dict, in_features: int, out_features: int,
+                           name: str = "projection") -> None:
+    """Raise ``ValueError`` when a canonical projection's tensors do not cover [out, in].
+
+    A store file cut short, or a blob that lies about the shape, is caught on
+    the host before any byte is staged or copied to the GPU.
+    """
+    numel = in_features * out_features
+    w = state.get("weight")
+    if w is None or w.numel() * 2 != numel:
+        got = None if w is None else w.numel()
+        raise ValueError(f"{name}: packed weight has {got} bytes, expected {numel // 2} "
+                         f"for [{out_features}, {in_features}]")
+    a = state.get("absmax")
+    if a is None or a.numel() * NF4_BLOCKSIZE != numel:
+        got = None if a is None else a.numel()
+        raise ValueError(f"{name}: absmax has {got} entries, expected {numel // NF4_BLOCKSIZE}")
+    c = state.get("code")
+    if c is None or c.numel() != 16:
+        raise ValueError(f"{name}: NF4 codebook must have 16 entries")
+    if is_nested(state):
+        a2 = state.get("state2_absmax")
+        need = -(-a.numel() // NESTED_BLOCKSIZE)
+        if a2 is None or a2.numel() < need or state.get("state2_code") is None:
+            raise ValueError(f"{name}: nested absmax state is incomplete")
+
+
+# ---------------------------------------------------------------------------
+# Store files (one safetensors file per expert)
+# ---------------------------------------------------------------------------
+
+def store_file_name(layer_id: int, expert_id: int) -> str:
+    """``layer_LL_expert_EE.safetensors`` (the reference's ``model/loader.py:305``)."""
+    return f"layer_{layer_id:02d}_expert_{expert_id:02d}.safetensors"
+
+
+def expert_store_tensors(expert) -> dict:
+    """Flat store dict ``{"w1.weight": ..., "w1.weight.absmax": ..., ...}`` of an expert.
+
+    ``expert`` exposes ``w1``/``w2``/``w3`` as serialized state dicts
+    (``PrequantizedNF4Expert``) or as modules with a ``.state`` dict
+    (``QuantizedMixtralExpert``'s projections).
+    """
+    out = {}
+    for proj in PROJECTIONS:
+        st = getattr(expert, proj)
+        st = st if isinstance(st, dict) else st.state
+        for key, t in st.items():
+            if isinstance(t, torch.Tensor):
+                out[f"{proj}.{key}"] = t.detach().to("cpu").contiguous()
+    return out
+
+
+def save_expert_store(store_dir, layer_id: int, expert_id: int, expert):
+    """Write one expert to ``store_dir`` in the store format; returns the file path."""
+    from pathlib import Path
+
+    from safetensors.torch import save_file
+
+    path = Path(store_dir) / store_file_name(layer_id, expert_id)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    save_file(expert_store_tensors(expert), str(path))
+    return path
+
+
 # ---------------------------------------------------------------------------
 # Quantizer (store writer; not on the inference path)
 # ---------------------------------------------------------------------------
@@ -146,6 +211,11 @@ def quantize_nf4_packed(weight: torch.Tensor, blocksize: int = NF4_BLOCKSIZE):
     idx = torch.bucketize(normed, mids, right=False, out_int32=True).to(torch.uint8)
     packed = ((idx[0::2] << 4) | idx[1::2]).contiguous()
     return packed, absmax, code
+
+
+def quantize_linear_state(weight: torch.Tensor, compress_statistics: bool = False) -> dict:
+    """Serialized NF4 state of one [out, in] weight (alias of :func:`quantize_nf4`)."""
+    return quantize_nf4(weight, compress_statistics=compress_statistics)
 
 
 def quantize_nf4(weight: torch.Tensor, compress_statistics: bool = False,

@@ -20,7 +20,7 @@ from typing import Optional
 
 import torch
 
-from moeinfra_b200.model.nf4_format import canonical_state
+from moeinfra_b200.model.nf4_format import canonical_state, check_projection_sizes
 from moeinfra_b200.transfer.pinned_memory import PinnedMemoryBudget
 
 SLAB_ALIGN = 256
@@ -173,6 +173,13 @@ class ReusablePinnedStagingPool:
         if not slot.in_use:
             raise RuntimeError("Slot must be acquired before staging")
         states = {n: self._projection_state(expert, n) for n in self._PROJECTIONS}
+        hidden = getattr(expert, "hidden_size", None)
+        inter = getattr(expert, "intermediate_size", None)
+        if hidden is not None and inter is not None:
+            # A short or mis-shaped store tensor fails here, on the host.
+            for n, (i_f, o_f) in (("w1", (hidden, inter)), ("w3", (hidden, inter)),
+                                  ("w2", (inter, hidden))):
+                check_projection_sizes(states[n], i_f, o_f, n)
         layout, nbytes = plan_layout(states)
         if nbytes > slot.size_bytes:
             raise ValueError(f"expert needs {nbytes} staging bytes, slot holds {slot.size_bytes}")

@@ -123,4 +123,8 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MOE_REFERENCE_ROOT", "/root/reference"))
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MOE_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py <path to the reference checkout> "
+                 "(or set MOE_REFERENCE_ROOT)")
+    main(root)

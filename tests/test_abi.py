@@ -40,7 +40,7 @@ def test_every_declared_symbol_is_exported_and_bound():
 
 
 def test_status_strings():
-    for code in range(7):
+    for code in range(8):
         assert _native.status_string(code) != "unknown status"
     assert _native.status_string(99) == "unknown status"
 
