@@ -176,24 +176,38 @@ class ClockSampler:
 # CPU baseline (the reference path restated on the host cores)
 # ----------------------------------------------------------------------------
 
-def cpu_layer_sample(steps: int, warmup: int, batch: int, time_budget_s: float | None):
-    """Time layer-0 steps of the workload with ``oracle.cpu_path`` on the host cores.
+def host_cores() -> int:
+    """Host threads this process may run on (torchrun sets OMP_NUM_THREADS=1; ignore it)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
 
-    Returns ``(tok_per_s for the 32-layer stack, seconds per layer step, steps run,
-    threads)``.  Weights are generated on the host with the same seeds and
-    quantizer (host RNG, so values differ from the device arm's; shapes and
-    distributions are the same).
+
+def cpu_layer_sample(steps: int, warmup: int, batch: int, time_budget_s: float | None):
+    """Time layer steps of the workload with ``oracle.cpu_path`` on every host core.
+
+    Step i runs ``batch`` new tokens through layer ``i % LAYERS`` (that layer's
+    gate; the eight experts' NF4 weights are layer 0's for every layer -- a
+    host-memory bound on the sample, stated in its description).  Returns
+    ``(tok_per_s of the 32-layer stack, list of per-step seconds, threads)``.
+    Weights are generated on the host with the device arm's seeds and
+    quantizer (host RNG, so values differ; shapes and distributions match).
     """
     from moeinfra_b200.model.nf4_format import NF4_CODE
     from oracle import cpu_path
-    threads = torch.get_num_threads()
+    threads = host_cores()
+    torch.set_num_threads(threads)
     code = torch.tensor(NF4_CODE, dtype=torch.float32)
-    gate = make_gate(0, "cpu")
+    gates = {}
     toks = make_tokens(steps + warmup, batch, "cpu")
     experts: dict[int, dict] = {}
 
     def step(i):
-        _, _, idx = cpu_path.route(toks[i], gate, TOP_K)
+        layer = i % LAYERS
+        if layer not in gates:
+            gates[layer] = make_gate(layer, "cpu")
+        _, _, idx = cpu_path.route(toks[i], gates[layer], TOP_K)
         table = [None] * EXPERTS
         for e in sorted(set(idx.reshape(-1).tolist())):
             if e not in experts:
@@ -201,7 +215,7 @@ def cpu_layer_sample(steps: int, warmup: int, batch: int, time_budget_s: float |
                 experts[e] = {n: {"q": q, "absmax": a} for n, (q, a, _) in st.items()}
             table[e] = experts[e]
         t0 = time.perf_counter()
-        cpu_path.layer_forward(toks[i], gate, table, code, HIDDEN, FFN, TOP_K)
+        cpu_path.layer_forward(toks[i], gates[layer], table, code, HIDDEN, FFN, TOP_K)
         return time.perf_counter() - t0
 
     for i in range(warmup):
@@ -212,7 +226,27 @@ def cpu_layer_sample(steps: int, warmup: int, batch: int, time_budget_s: float |
         if time_budget_s is not None and sum(times) > time_budget_s and len(times) >= 2:
             break
     per_layer = sum(times) / len(times)
-    return batch / (per_layer * LAYERS), per_layer, len(times), threads
+    return batch / (per_layer * LAYERS), times, threads
+
+
+def cpu_sample_text(times: list, batch: int) -> str:
+    per_layer = sum(times) / len(times)
+    return (f"{len(times)} steps, each {batch} token(s) through one of the {LAYERS} MoE layers "
+            f"(that layer's gate; layer 0's NF4 experts stand in for every layer's); "
+            f"{per_layer:.3f} s per layer step; value = tokens / ({LAYERS} x mean layer-step "
+            f"time); oracle.cpu_path torch CPU restatement")
+
+
+def config_dict(L: int, B: int, world: int) -> dict:
+    """The workload description, identical in the device and reference arms."""
+    return {
+        "workload": f"config 1 (Mixtral MoE layer decode) over a {L}-layer MoE stack, "
+                    f"bs{B} per GPU",
+        "batch_per_gpu": B, "global_batch": B * world, "layers": L, "hidden": HIDDEN,
+        "ffn": FFN, "experts": EXPERTS, "top_k": TOP_K, "parallelism": f"ep{world}",
+        "l2": "inputs larger than L2: every step streams each layer's routed experts "
+              "(99 MB each, 126 MB L2) once, 32 layers per step",
+    }
 
 
 # ----------------------------------------------------------------------------
@@ -290,6 +324,7 @@ def run_device(args, rank: int, world: int, local_rank: int):
                                                local, rank=rank, world_size=world,
                                                max_tokens=B))
         step_fn = ep_layers
+        owned_experts = owned
     torch.cuda.synchronize()
     _barrier(world)
 
@@ -420,9 +455,14 @@ def run_device(args, rank: int, world: int, local_rank: int):
                 "launch_us": round(per_launch_s * 1e6, 2), "peak_source": peak[1]}
         del g2
 
+    if world > 1:
+        roof = ep_roofline(step_fn, tokens[W], dev, L, K)
+        e2e = ep_e2e(step_fn, tokens, dev, L, K, W, world)
+        ep_par = ep_parity(step_fn[0], tokens[0], dev, rank)
+
     # --- end to end through the public API, host buffers -----------------------------
-    e2e = None
     if world == 1:
+        e2e = None
         host_in = torch.empty(K + W, B, HIDDEN, dtype=torch.float16).pin_memory()
         host_in.copy_(tokens.cpu())
         host_out = torch.empty(B, HIDDEN, dtype=torch.float16).pin_memory()
@@ -456,36 +496,166 @@ def run_device(args, rank: int, world: int, local_rank: int):
         "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
         "data": "synthetic: seeded N(0,0.02) weights NF4-quantized on device; N(0,1) fp16 tokens",
-        "config": {
-            "workload": f"config 1 (Mixtral MoE layer decode) over a {L}-layer MoE stack, "
-                        f"bs{B} per GPU",
-            "batch_per_gpu": B, "global_batch": B * world, "layers": L, "hidden": HIDDEN,
-            "ffn": FFN, "experts": EXPERTS, "top_k": TOP_K,
-            "parallelism": f"ep{world}",
-            "l2": "inputs larger than L2: every step streams each layer's routed experts "
-                  "(99 MB each, 126 MB L2) once, 32 layers per step",
-        },
+        "config": config_dict(L, B, world),
         "gpu_launches": int(launches_per_step * K),
         "clocks": clk,
     }
+    line["roofline"] = roof
+    line["e2e"] = e2e
     if world == 1:
         line["hbm_gbs_step"] = round(routed_experts * EXPERT_BYTES / (ms / 1e3) / 1e9, 1)
-        line["roofline"] = roof
-        line["e2e"] = e2e
         if not args.no_extra:
             line.update(measure_batches(gates, tables, dev, L, K))
+            line["config0"] = measure_config0(tables, dev, K)
+    else:
+        line["ep_parity"] = ep_par
+    # Kernels flag timed-out waits or codebook mismatches on the device: a run
+    # whose launches were invalid must not print a number.
+    from moeinfra_b200 import kernels as _k
+    _k.check_device(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tps, per_layer, n, thr = cpu_layer_sample(steps=args.cpu_steps, warmup=1, batch=B,
-                                                  time_budget_s=20.0)
+        tps, times, thr = cpu_layer_sample(steps=args.cpu_steps, warmup=1, batch=B,
+                                           time_budget_s=20.0)
         line["cpu_baseline"] = {"value": round(tps, 5), "unit": "tok/s", "cores": thr,
-                                "kind": "port",
-                                "sample": f"{n} steps of layer 0 at bs{B} (of {L} layers; "
-                                          f"{per_layer:.3f} s per layer step), oracle.cpu_path "
-                                          "torch CPU restatement"}
+                                "kind": "port", "sample": cpu_sample_text(times, B)}
     if graph is not None:
         graph.reset()  # a graph holding NCCL calls must go before the process group
         del graph
     return line
+
+
+def ep_roofline(ep_layers, tok, dev, L: int, K: int):
+    """Per-GPU roofline of the local expert stage of the expert-parallel step.
+
+    The rows each rank's experts receive for one step's tokens are produced
+    once (router, dispatch, all-to-all); then the local expert stage alone
+    (``moe_experts_forward``) is replayed over the L layers in a CUDA graph.
+    Algorithmic bytes = this rank's experts that received rows x 99,090,624 B
+    (+ rows in/out), per layer.
+    """
+    from moeinfra_b200 import kernels
+    calls, nbytes = [], 0
+    for lay in ep_layers:
+        x_sorted, local_off = lay.received_rows(tok)
+        off = local_off.tolist()
+        active = sum(1 for j in range(len(off) - 1) if off[j + 1] > off[j])
+        rows = off[-1]
+        nbytes += active * EXPERT_BYTES + 2 * rows * HIDDEN * 2
+        calls.append((lay, local_off, x_sorted))
+    def stage():
+        for lay, off_t, xs in calls:
+            kernels.experts_forward(lay._table, off_t, xs, HIDDEN, FFN)
+    reps = max(3, K // 2)
+    ms = _graph_time(stage, reps, dev) / L
+    achieved = nbytes / L / (ms / 1e3) / 1e9
+    peak = _measured_peak("hbm_gbs")
+    world = torch.distributed.get_world_size()
+    vals = torch.tensor([achieved, ms], dtype=torch.float64, device=dev)
+    lo = vals.clone()
+    torch.distributed.all_reduce(lo, op=torch.distributed.ReduceOp.MIN)
+    return {"bound": "hbm", "achieved": round(float(lo[0]), 1), "peak": peak[0], "unit": "GB/s",
+            "frac": round(float(lo[0]) / peak[0], 4), "traffic": None,
+            "kernel": f"local expert stage per GPU (moe_experts_forward on the rows this rank's "
+                      f"{EXPERTS // world} expert(s) received), per layer; min over ranks",
+            "algorithmic_bytes_per_launch": int(nbytes / L), "launch_us": round(ms * 1e3, 2),
+            "peak_source": peak[1]}
+
+
+def ep_e2e(ep_layers, tokens, dev, L: int, K: int, W: int, world: int):
+    """The expert-parallel step through its public call, host buffers in and out."""
+    B = tokens.shape[1]
+    host_in = torch.empty(K + W, B, HIDDEN, dtype=torch.float16).pin_memory()
+    host_in.copy_(tokens.cpu())
+    host_out = torch.empty(B, HIDDEN, dtype=torch.float16).pin_memory()
+    h_dev = torch.empty(B, HIDDEN, dtype=torch.float16, device=dev)
+
+    def step(i):
+        h_dev.copy_(host_in[i], non_blocking=True)
+        y = None
+        for lay in ep_layers:
+            y = lay.forward(h_dev)
+        host_out.copy_(y, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize()
+    _barrier(world)
+    a, b = _events()
+    a.record()
+    for i in range(W, W + K):
+        step(i)
+    b.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(a.elapsed_time(b), world, dev)
+    return {"value": round(B * K * world / (ms / 1e3), 3), "unit": "tok/s",
+            "h2d_bytes_per_step": B * HIDDEN * 2, "d2h_bytes_per_step": B * HIDDEN * 2,
+            "api": "ExpertParallelMoE.forward per layer (eager, NCCL all-to-all), pinned host "
+                   "in/out per rank; max over ranks"}
+
+
+def ep_parity(ep_layer0, tok, dev, rank: int):
+    """Layer 0 on every rank: the expert-parallel output vs the single-GPU layer.
+
+    Each rank builds all eight experts of layer 0 locally and runs the fused
+    single-GPU layer on its own tokens; the expert-parallel path must agree
+    within the layer tolerance (rel-L2 <= 2e-3, max-abs <= 1e-2 x max(1,|ref|);
+    per-expert token counts differ between the two, which can switch an
+    expert between the 1-row and multi-row semantics).  Worst over ranks.
+    """
+    from moeinfra_b200 import kernels
+    full = [resident_expert(0, e, dev) for e in range(EXPERTS)]
+    table = kernels.expert_array([x.nf4_descriptor for x in full])
+    want, idx, _ = kernels.layer_forward(tok, ep_layer0.router.gate_f16(), table, TOP_K, HIDDEN,
+                                         FFN)
+    got = ep_layer0.forward(tok)
+    torch.cuda.synchronize()
+    d = (got.float() - want.float())
+    rel = float(d.norm() / max(float(want.float().norm()), 1e-30))
+    mabs = float(d.abs().max())
+    scale = max(1.0, float(want.float().abs().max()))
+    ok = 1.0 if (rel <= 2e-3 and mabs <= 1e-2 * scale) else 0.0
+    v = torch.tensor([rel, mabs, -ok], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(v, op=torch.distributed.ReduceOp.MAX)
+    del full, table
+    return {"max_abs": float(v[1]), "rel_l2": float(v[0]), "ok": bool(v[2] < 0),
+            "check": "layer 0, each rank's step-0 tokens: expert-parallel vs single-GPU fused "
+                     "layer with all 8 experts local; worst over ranks"}
+
+
+def measure_config0(tables, dev, K: int):
+    """Config 0: one Mixtral expert, 16 tokens (``moe_expert_forward``).
+
+    Eight different experts (layer 0's) are cycled so that no expert is
+    reused while it could still sit in L2 (99 MB each, 126 MB L2).
+    """
+    from moeinfra_b200 import _native, kernels
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(16, HIDDEN, generator=g, device=dev).to(torch.float16)
+    descs = [tables[0][e] for e in range(EXPERTS)]
+    ys = [torch.empty_like(x) for _ in descs]
+    lib = _native.lib()
+    ws_bytes = lib.moe_expert_workspace_size(16, HIDDEN, FFN)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    import ctypes
+
+    def run():
+        s = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        for d, y in zip(descs, ys):
+            _native.check(lib.moe_expert_forward(ctypes.byref(d), ctypes.c_void_p(x.data_ptr()),
+                                                 16, HIDDEN, FFN, ctypes.c_void_p(y.data_ptr()),
+                                                 ctypes.c_void_p(ws.data_ptr()), ws_bytes, s),
+                          "moe_expert_forward")
+    ms = _graph_time(run, max(3, K // 2), dev) / len(descs)
+    nbytes = EXPERT_BYTES + 2 * 16 * HIDDEN * 2
+    peak = _measured_peak("hbm_gbs")
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {"value": round(gbs, 1), "unit": "GB/s", "us_per_expert": round(ms * 1e3, 2),
+            "tokens": 16, "algorithmic_bytes": nbytes,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak[0],
+                         "unit": "GB/s", "frac": round(gbs / peak[0], 4),
+                         "peak_source": peak[1]},
+            "note": "single SwiGLU expert (hidden 4096, ffn 14336) on 16 fp16 tokens"}
 
 
 def _graph_time(fn, reps: int, dev) -> float:
@@ -586,20 +756,24 @@ def _measured_peak(key: str):
         return fallback[key], "fallback"
 
 
-def run_reference(args):
-    tps, per_layer, n, thr = cpu_layer_sample(steps=args.steps, warmup=args.warmup,
-                                              batch=args.batch, time_budget_s=None)
-    sample = (f"{n} steps of layer 0 at bs{args.batch} (of {args.layers} layers), "
-              f"{per_layer:.3f} s per layer step, oracle.cpu_path torch CPU restatement")
+def run_reference(args, world: int):
+    """The reference's CPU path (its restatement) on the host cores, for this arm's workload.
+
+    One step = the job's ``batch x world`` tokens through one MoE layer (a
+    bounded sample of the 32-layer step; ``ms_per_step`` is that measured
+    time), value = tokens / (32 x mean layer-step time).
+    """
+    B = args.batch * world
+    tps, times, thr = cpu_layer_sample(steps=args.steps, warmup=args.warmup, batch=B,
+                                       time_budget_s=None)
+    sample = cpu_sample_text(times, B)
     return {
-        "metric": METRIC, "value": round(tps, 5), "unit": "tok/s", "n_gpus": 1,
-        "steps": n, "warmup": args.warmup, "ms_per_step": round(per_layer * args.layers * 1e3, 3),
+        "metric": METRIC, "value": round(tps, 5), "unit": "tok/s", "n_gpus": world,
+        "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": round(sum(times) / len(times) * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
         "data": "synthetic: seeded N(0,0.02) weights NF4-quantized on host; N(0,1) fp16 tokens",
-        "config": {"workload": f"config 1 (Mixtral MoE layer decode) over a {args.layers}-layer "
-                               f"MoE stack, bs{args.batch}", "batch_per_gpu": args.batch,
-                   "layers": args.layers, "hidden": HIDDEN, "ffn": FFN, "experts": EXPERTS,
-                   "top_k": TOP_K, "parallelism": "cpu"},
+        "config": config_dict(args.layers, args.batch, world),
         "impl": "reference",
         "cpu_baseline": {"value": round(tps, 5), "unit": "tok/s", "cores": thr, "kind": "port",
                          "sample": sample},
@@ -639,8 +813,9 @@ def main():
         os.write(json_fd, (json.dumps(line) + "\n").encode())
 
     if args.impl == "reference":
+        # Under torchrun rank 0 alone runs the CPU sample; the other ranks exit.
         if rank == 0:
-            emit(run_reference(args))
+            emit(run_reference(args, world))
         return 0
 
     if world > 1:

@@ -74,13 +74,7 @@ class ExpertParallelMoE:
     def __call__(self, h: torch.Tensor) -> torch.Tensor:
         return self.forward(h)
 
-    @torch.no_grad()
-    def forward(self, h: torch.Tensor) -> torch.Tensor:
-        if h.ndim != 2 or h.shape[1] != self.hidden:
-            raise ValueError(f"expected [tokens, {self.hidden}] fp16, got {tuple(h.shape)}")
-        if h.shape[0] > self.max_tokens:
-            raise ValueError(f"{h.shape[0]} tokens exceed max_tokens={self.max_tokens}")
-        h = h.contiguous()
+    def _dispatch(self, h: torch.Tensor):
         E, G, cap, k = self.num_experts, self.world, self.cap, self.top_k
         _, w, idx = kernels.router_topk(h, self.router.gate_f16(), k, with_logits=False)
         offsets, pair_token, _, pair_slot = kernels.permute(idx, w, E)
@@ -88,6 +82,23 @@ class ExpertParallelMoE:
         recv = torch.empty_like(send)
         dist.all_to_all_single(recv, send, group=self.group)  # rows + count headers
         x_sorted, local_off, recv_counts = kernels.ep_receive(recv, E, G, cap)
+        return x_sorted, local_off, recv_counts, slot_ep, idx, w
+
+    @torch.no_grad()
+    def received_rows(self, h: torch.Tensor):
+        """``(x_sorted, local_offsets)``: the rows this rank's experts get for ``h`` (collective)."""
+        x_sorted, local_off, _, _, _, _ = self._dispatch(h.contiguous())
+        return x_sorted, local_off
+
+    @torch.no_grad()
+    def forward(self, h: torch.Tensor) -> torch.Tensor:
+        if h.ndim != 2 or h.shape[1] != self.hidden:
+            raise ValueError(f"expected [tokens, {self.hidden}] fp16, got {tuple(h.shape)}")
+        if h.shape[0] > self.max_tokens:
+            raise ValueError(f"{h.shape[0]} tokens exceed max_tokens={self.max_tokens}")
+        h = h.contiguous()
+        E, G, cap = self.num_experts, self.world, self.cap
+        x_sorted, local_off, recv_counts, slot_ep, idx, w = self._dispatch(h)
         y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden, self.inter)
         y_back = kernels.ep_return(y_sorted, recv_counts, E, G, cap)
         y_home = torch.empty_like(y_back)

@@ -35,14 +35,18 @@ class MoELayer:
     """Single Mixtral MoE layer with expert offloading."""
 
     def __init__(self, layer_id: int, router, cache_manager, model_loader, transfer_scheduler,
-                 logger: Optional[logging.Logger] = None) -> None:
+                 logger: Optional[logging.Logger] = None, prefetch_engine=None) -> None:
         self.layer_id = layer_id
         self.router = router
         self.cache_manager = cache_manager
         self.model_loader = model_loader
         self.transfer_scheduler = transfer_scheduler
+        self.prefetch_engine = prefetch_engine
         self._logger = logger or logging.getLogger(__name__)
         self._desc_cache: Optional[tuple] = None
+        # Routing of the last offloaded call (device int64 [T, k]); None after a
+        # resident call.  The engine hands it to the prefetcher.
+        self.last_expert_indices: Optional[torch.Tensor] = None
 
     # -- residency (reference :39-115) -------------------------------------------
     def _ensure_expert_on_gpu(self, expert_id: int):
@@ -53,6 +57,14 @@ class MoELayer:
             self.cache_manager.put(self.layer_id, expert_id, expert, device="cpu")
         if expert.device.type == "cuda":
             return expert
+        # A prefetch of this expert may already be on the copy stream: adopt it.
+        adopt = getattr(self.transfer_scheduler, "adopt_async", None)
+        if adopt is not None:
+            adopted = adopt(self.layer_id, expert_id)
+            if adopted is not None:
+                if self.prefetch_engine is not None:
+                    self.prefetch_engine.forget(self.layer_id, expert_id)
+                return adopted
         request = TransferRequest(
             request_id=f"layer-{self.layer_id}-expert-{expert_id}-{id(self)}",
             layer_id=self.layer_id, expert_id=expert_id,
@@ -138,9 +150,11 @@ class MoELayer:
 
         table = self._resident_table()
         if table is not None:
+            self.last_expert_indices = None
             return self._fused(hidden_states, table, self._desc_cache[2][0].intermediate_size)
 
         expert_indices, expert_weights = self.router.route(hidden_states)
+        self.last_expert_indices = expert_indices
         unique_ids = sorted(int(e) for e in expert_indices.reshape(-1).unique().tolist())
         was_resident = {
             e: (self.cache_manager.is_gpu_resident(self.layer_id, e)

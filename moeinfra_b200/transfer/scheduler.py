@@ -234,6 +234,31 @@ class TransferScheduler:
         self._async_in_flight[key] = handle
         return handle
 
+    def adopt_async(self, layer_id: int, expert_id: int):
+        """Take over an in-flight asynchronous copy now; returns the GPU expert or ``None``.
+
+        The caller needs the expert before the copy has been polled complete:
+        the current stream waits on the copy's event (no host wait), the expert
+        is reconstructed and cached as :meth:`poll_async` would.  ``None`` when
+        no live (non-cancelled) copy of this expert is in flight.
+        """
+        key = (layer_id, expert_id)
+        handle = self._async_in_flight.get(key)
+        if handle is None or handle.status != TransferStatus.IN_FLIGHT:
+            return None
+        torch.cuda.current_stream().wait_event(handle.event)
+        try:
+            expert = ReconstructedNF4Expert(handle.cpu_expert, handle.gpu_state)
+            self._cache_manager.put(layer_id, expert_id, expert,
+                                    device=f"cuda:{torch.cuda.current_device()}")
+            handle.status = TransferStatus.READY
+            self._bw_monitor.record(self._cache_manager.get_size_bytes(layer_id, expert_id))
+            return expert
+        finally:
+            self._staging_pool.mark_transfer_complete(handle.slot, self._transfer_stream)
+            self._staging_pool.release(handle.slot)
+            del self._async_in_flight[key]
+
     def poll_async(self, layer_id: int, expert_id: int) -> TransferStatus:
         key = (layer_id, expert_id)
         handle = self._async_in_flight.get(key)
