@@ -459,6 +459,7 @@ def run_device(args, rank: int, world: int, local_rank: int):
         roof = ep_roofline(step_fn, tokens[W], dev, L, K)
         e2e = ep_e2e(step_fn, tokens, dev, L, K, W, world)
         ep_par = ep_parity(step_fn[0], tokens[0], dev, rank)
+        ep_split = ep_breakdown(step_fn, tokens[W], dev, L, K, world)
 
     # --- end to end through the public API, host buffers -----------------------------
     if world == 1:
@@ -509,6 +510,7 @@ def run_device(args, rank: int, world: int, local_rank: int):
             line["config0"] = measure_config0(tables, dev, K)
     else:
         line["ep_parity"] = ep_par
+        line["ep_breakdown"] = ep_split
     # Kernels flag timed-out waits or codebook mismatches on the device: a run
     # whose launches were invalid must not print a number.
     from moeinfra_b200 import kernels as _k
@@ -559,6 +561,29 @@ def ep_roofline(ep_layers, tok, dev, L: int, K: int):
                       f"{EXPERTS // world} expert(s) received), per layer; min over ranks",
             "algorithmic_bytes_per_launch": int(nbytes / L), "launch_us": round(ms * 1e3, 2),
             "peak_source": peak[1]}
+
+
+def ep_breakdown(ep_layers, tok, dev, L: int, K: int, world: int):
+    """Where an expert-parallel layer's time goes, each variant a CUDA graph of L layers.
+
+    full: the step as timed; kernels: the same kernels with both all-to-alls
+    replaced by local copies; a2a: the two NCCL all-to-alls per layer alone on
+    buffers of the same shapes.  Per layer, max over ranks.
+    """
+    reps = max(3, K // 2)
+    h = tok.contiguous()
+    bufs = [lay.exchange_buffers(h.shape[0]) for lay in ep_layers]
+    out = {}
+    for name, fn in (
+            ("layer_us", lambda: [lay.forward(h) for lay in ep_layers]),
+            ("kernels_only_us", lambda: [lay.forward(h, exchange=False) for lay in ep_layers]),
+            ("a2a_only_us", lambda: [lay.exchange_only(b) for lay, b in zip(ep_layers, bufs)])):
+        _barrier(world)
+        ms = _graph_time(fn, reps, dev) / L
+        out[name] = round(_max_over_ranks(ms, world, dev) * 1e3, 2)
+    out["note"] = ("per layer, CUDA graphs of the 32-layer step; kernels_only replaces the two "
+                   "NCCL all-to-alls by local copies, a2a_only runs just the two all-to-alls")
+    return out
 
 
 def ep_e2e(ep_layers, tokens, dev, L: int, K: int, W: int, world: int):

@@ -57,8 +57,15 @@ constexpr uint32_t kLutBytes = 256 * 16 * 8;        // byte -> (code hi, code lo
 constexpr uint32_t kLutWin = 0x10000;
 MOE_DEFINE_ERROR_WORD()
 
-// kNarrow: tiles of at most 64 tokens (one TMA box), whose token slot is a
-// quarter of the wide one, so more stages fit and hide the per-stage hand-off.
+// kNarrow: tiles of at most 32 tokens.  Their weights are decoded straight to
+// bf16: fp16(bf16(code * absmax)) -- the reference's multi-row weight -- equals
+// bf16(code * absmax) exactly, so the MMA takes A as bf16 and skips the fp16
+// widening (4 instead of 7 instructions per packed byte).  The tokens then go
+// in as bf16 too, each fp16 row x split into two bf16 rows hi = bf16(x),
+// lo = bf16(x - hi) (exact: an fp16 significand has 11 bits, hi takes 8, the
+// remainder at most 3), and the epilogue adds the two accumulator columns of a
+// token: every product is exact and accumulates in fp32, as in the fp16 GEMM.
+// The split rows (2 x 32 per tile) fill one TMA box, as 64 fp16 rows did.
 // Narrow tiles, and the down projection of wide ones, keep the dequantized
 // weights (A) in tensor memory: the dequant threads (one weight row each)
 // write them with tcgen05.st and the MMA reads A from TMEM, so A never crosses
@@ -69,15 +76,17 @@ MOE_DEFINE_ERROR_WORD()
 template <bool kGate, bool kNarrow>
 struct Cfg {
   static constexpr int kMats = kGate ? 2 : 1;
-  static constexpr int kTileN = kNarrow ? kBoxRows : kMaxN;
+  static constexpr bool kSplit = kNarrow;                 // tokens as bf16 hi/lo rows
+  static constexpr int kTileN = kNarrow ? kBoxRows / 2 : kMaxN;  // tokens per tile
+  static constexpr int kBRows = kSplit ? 2 * kTileN : kTileN;    // B rows per tile
   static constexpr bool kATmem = kNarrow || !kGate;
   static constexpr int kStages = kNarrow ? (kGate ? 6 : 7) : (kGate ? 3 : 6);
   // K steps of packed codes in flight per dequant thread.
   static constexpr int kPrefetch = kNarrow ? (kGate ? 6 : 8) : 4;
   static constexpr uint32_t kAStage = kATmem ? 0 : kMats * kATile;  // A bytes in a smem stage
-  static constexpr uint32_t kStage = kAStage + (uint32_t)kTileN * kBK * 2;
-  static constexpr uint32_t kDCol3 = kNarrow ? kTileN : 256;       // W3 accumulator column
-  static constexpr uint32_t kACol = kATmem ? kMats * kTileN : 0;  // first A column
+  static constexpr uint32_t kStage = kAStage + (uint32_t)kBRows * kBK * 2;
+  static constexpr uint32_t kDCol3 = kNarrow ? kBRows : 256;       // W3 accumulator column
+  static constexpr uint32_t kACol = kATmem ? kMats * kBRows : 0;  // first A column
   static constexpr uint32_t kTmemCols = 512;
   static constexpr bool kLutWindow = kNarrow;
   // Wide: stages, table, alignment slack.  Narrow: everything below the
@@ -179,6 +188,27 @@ __device__ __forceinline__ uint32_t decode_byte_w(uint32_t w, uint32_t lut_lane,
       : "r"(w), "r"(lut_lane), "n"(0x7604 | (K << 4)), "l"(am2));
   return out;
 }
+// Byte K of w -> bf16 pair (element 2j low) of bf16(code * absmax): table
+// address, the two fp32 codes, one packed multiply, one packed rounding.
+template <int K>
+__device__ __forceinline__ uint32_t decode_byte_bf16(uint32_t w, uint32_t lut_lane, uint64_t am2) {
+  uint32_t out;
+  asm("{\n .reg .b32 ad, lo, hi;\n .reg .b64 c, p;\n"
+      " prmt.b32 ad, %1, %2, %3;\n"
+      " ld.shared.b64 c, [ad];\n"
+      " mul.rn.f32x2 p, c, %4;\n"
+      " mov.b64 {lo, hi}, p;\n"
+      " cvt.rn.bf16x2.f32 %0, hi, lo;\n}\n"
+      : "=r"(out)
+      : "r"(w), "r"(lut_lane), "n"(0x7604 | (K << 4)), "l"(am2));
+  return out;
+}
+// fp16 value -> its exact bf16 hi/lo pair (hi = bf16(v), lo = bf16(v - hi)).
+__device__ __forceinline__ void split_bf16(float v, uint16_t* hi, uint16_t* lo) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  *hi = __bfloat16_as_ushort(h);
+  *lo = __bfloat16_as_ushort(__float2bfloat16_rn(__fsub_rn(v, __bfloat162float(h))));
+}
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -270,9 +300,11 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// Instruction descriptor: fp32 accumulate, fp16 A and B, both K-major, M=128, N.
-__device__ __forceinline__ uint32_t instr_desc(int n) {
-  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+// Instruction descriptor: fp32 accumulate, fp16 (or bf16) A and B, both
+// K-major, M=128, N.
+__device__ __forceinline__ uint32_t instr_desc(int n, bool bf16) {
+  const uint32_t ab = bf16 ? ((1u << 7) | (1u << 10)) : 0u;
+  return (1u << 4) | ab | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
 
 // Tile t of this launch -> expert e, first weight row m0, first token n0, tokens nt.
@@ -449,7 +481,12 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
               uint32_t h[kWords * 4];
 #pragma unroll
               for (int cc = 0; cc < kWords; ++cc) {
-                if constexpr (C::kLutWindow) {
+                if constexpr (C::kSplit) {
+                  h[cc * 4 + 0] = decode_byte_bf16<0>(qv[d][m][cc], lut_lane, am2);
+                  h[cc * 4 + 1] = decode_byte_bf16<1>(qv[d][m][cc], lut_lane, am2);
+                  h[cc * 4 + 2] = decode_byte_bf16<2>(qv[d][m][cc], lut_lane, am2);
+                  h[cc * 4 + 3] = decode_byte_bf16<3>(qv[d][m][cc], lut_lane, am2);
+                } else if constexpr (C::kLutWindow) {
                   h[cc * 4 + 0] = decode_byte_w<0>(qv[d][m][cc], lut_lane, am2);
                   h[cc * 4 + 1] = decode_byte_w<1>(qv[d][m][cc], lut_lane, am2);
                   h[cc * 4 + 2] = decode_byte_w<2>(qv[d][m][cc], lut_lane, am2);
@@ -501,7 +538,8 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
         break;
       }
       tc_fence_after();
-      const int nchunk = (tl.nt + 15) / 16;
+      constexpr int kTokPerChunk = C::kSplit ? 8 : 16;  // a 16-column chunk
+      const int nchunk = (tl.nt + kTokPerChunk - 1) / kTokPerChunk;
       const uint32_t lane_addr = tmem + ((uint32_t)(rw * 32) << 16);
       for (int ch = part; ch < nchunk; ch += kParts) {
         uint32_t d1[16], d3[16];
@@ -510,16 +548,31 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
         tmem_wait_ld();
         const int row = tl.m0 + i;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = ch * 16 + j;
+        for (int j = 0; j < kTokPerChunk; ++j) {
+          const int n = ch * kTokPerChunk + j;
           if (n < tl.nt) {
             const int64_t p = s_off[tl.e] + tl.n0 + n;
-            uint16_t o;
-            if (kGate)
-              o = swiglu_f16(f2h(__uint_as_float(d1[j])), f2h(__uint_as_float(d3[j])));
-            else
-              o = f2h(__uint_as_float(d1[j]));
-            a.out[p * a.rows + row] = o;
+            float g, u = 0.f;
+            if constexpr (C::kSplit) {  // token n's hi and lo columns
+              g = __fadd_rn(__uint_as_float(d1[2 * j]), __uint_as_float(d1[2 * j + 1]));
+              if (kGate) u = __fadd_rn(__uint_as_float(d3[2 * j]), __uint_as_float(d3[2 * j + 1]));
+            } else {
+              g = __uint_as_float(d1[j]);
+              if (kGate) u = __uint_as_float(d3[j]);
+            }
+            if (kGate) {
+              const uint16_t o = swiglu_f16(f2h(g), f2h(u));
+              if constexpr (C::kSplit) {  // h feeds the down projection as hi/lo rows
+                uint16_t hi, lo;
+                split_bf16(h2f(o), &hi, &lo);
+                a.out[(2 * p) * a.rows + row] = hi;
+                a.out[(2 * p + 1) * a.rows + row] = lo;
+              } else {
+                a.out[p * a.rows + row] = o;
+              }
+            } else {
+              a.out[p * a.rows + row] = f2h(g);
+            }
           }
         }
       }
@@ -533,8 +586,9 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
       uint32_t g = 0;
       for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x) {
         const Tile tl = tile_of<C::kTileN>(t, s_base, s_off, a.E, mtiles);
-        const int nbox = (tl.nt + kBoxRows - 1) / kBoxRows;
-        const int row0 = s_off[tl.e] + tl.n0;
+        const int brows = C::kSplit ? 2 * tl.nt : tl.nt;
+        const int nbox = (brows + kBoxRows - 1) / kBoxRows;
+        const int row0 = (C::kSplit ? 2 : 1) * (s_off[tl.e] + tl.n0);
         for (int kb = 0; kb < nblk; ++kb, ++g) {
           const int s = g % NS;
           if (!s_abort && !mbar_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1, a.wait_ns)) s_abort = 1;
@@ -558,8 +612,8 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
       bool issued_any = false;
       for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x, ++it) {
         const Tile tl = tile_of<C::kTileN>(t, s_base, s_off, a.E, mtiles);
-        const int n = (tl.nt + 15) & ~15;
-        const uint32_t idesc = instr_desc(n);
+        const int n = ((C::kSplit ? 2 * tl.nt : tl.nt) + 15) & ~15;
+        const uint32_t idesc = instr_desc(n, C::kSplit);
         if (!mbar_wait(saddr(&s_accempty), (it & 1) ^ 1, a.wait_ns)) {
           s_abort = 1;
           break;
@@ -627,16 +681,32 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Token matrix [rows_total, K] fp16, row-major: boxes of 64 rows x 64 K with
-// the 128-byte swizzle the UMMA K-major descriptor expects.
-bool make_token_map(CUtensorMap* map, const uint16_t* x, int64_t rows_total, int K) {
+// fp16 rows [P, K] -> bf16 rows [2P, K]: row 2p = bf16(x_p), row 2p+1 = the
+// exact remainder (the token operand of narrow tiles).
+__global__ void k_split_rows(const uint16_t* __restrict__ x, int64_t n, int K,
+                             uint16_t* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = i / K;
+    const int c = static_cast<int>(i - p * K);
+    uint16_t hi, lo;
+    split_bf16(h2f(x[i]), &hi, &lo);
+    out[(2 * p) * K + c] = hi;
+    out[(2 * p + 1) * K + c] = lo;
+  }
+}
+
+// Token matrix [rows_total, K] (fp16, or bf16 split rows), row-major: boxes of
+// 64 rows x 64 K with the 128-byte swizzle the UMMA K-major descriptor expects.
+bool make_token_map(CUtensorMap* map, const uint16_t* x, int64_t rows_total, int K, bool bf16) {
   auto fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows_total};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
   const cuuint32_t box[2] = {kBK, kBoxRows};
   const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box,
+  return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+            const_cast<uint16_t*>(x), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -657,16 +727,20 @@ int launch_dq(const GemmArgs& a, const CUtensorMap& map, cudaStream_t s) {
   return MOE_OK;
 }
 
-// Narrow tiles (on average at most 64 tokens per expert): 16 dequant warps,
-// 64-token tiles (an expert with more tokens takes several), deeper pipeline.
+// Narrow tiles (on average at most 32 tokens per expert): 16 dequant warps,
+// 32-token tiles of split bf16 rows (an expert with more tokens takes several),
+// deeper pipeline.  Wide tiles: 8 dequant warps, 256-token fp16 tiles.
 template <bool kGate>
-int launch_one(const GemmArgs& a, const uint16_t* x, int64_t P, cudaStream_t s) {
+int launch_one(const GemmArgs& a, const uint16_t* x, int64_t P, bool narrow, cudaStream_t s) {
   CUtensorMap map;
-  if (!make_token_map(&map, x, P, a.K)) return MOE_ERR_CUDA;
-  return P <= (int64_t)64 * a.E ? launch_dq<kGate, 16>(a, map, s) : launch_dq<kGate, 8>(a, map, s);
+  if (!make_token_map(&map, x, narrow ? 2 * P : P, a.K, narrow)) return MOE_ERR_CUDA;
+  return narrow ? launch_dq<kGate, 16>(a, map, s) : launch_dq<kGate, 8>(a, map, s);
 }
 
 }  // namespace
+
+// Narrow (split bf16) tiles when the experts average at most 32 tokens.
+bool gemm_narrow(int64_t P, int E) { return P <= (int64_t)32 * E; }
 
 // Shapes the tensor-core path accepts: weight rows (I and H) multiples of 128,
 // K extents multiples of 64, K-major 16-byte-aligned operands.
@@ -675,10 +749,12 @@ bool gemm_supported(int hidden, int inter) {
          inter % kBK == 0;
 }
 
+// h_sorted: [P, inter] fp16 (wide) or [2P, inter] bf16 split rows (narrow);
+// x_split: [2P, hidden] bf16, used (and required) only for narrow tiles.
 int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
                                 const int32_t* expert_offsets, const uint16_t* x_sorted,
                                 int64_t P, int hidden, int inter, uint16_t* h_sorted,
-                                uint16_t* y_sorted, cudaStream_t s) {
+                                uint16_t* y_sorted, uint16_t* x_split, cudaStream_t s) {
   if (E < 1 || E > MOE_MAX_EXPERTS || P < 1) return MOE_ERR_INVALID_ARG;
   if (!gemm_supported(hidden, inter)) return MOE_ERR_UNSUPPORTED;
   if (P > INT32_MAX / 2) return MOE_ERR_UNSUPPORTED;
@@ -697,12 +773,23 @@ int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
   a.rows = inter;
   a.out = h_sorted;
   a.wait_ns = wait_limit_ns();
-  int st = launch_one<true>(a, x_sorted, P, s);
+  const bool narrow = gemm_narrow(P, E);
+  const uint16_t* x_in = x_sorted;
+  if (narrow) {
+    if (!x_split || !aligned16(x_split)) return MOE_ERR_WORKSPACE;
+    const int64_t n = P * hidden;
+    const int64_t blocks = ceil_div(n, 256);
+    const int grid = static_cast<int>(blocks < sm_count() * 8 ? blocks : sm_count() * 8);
+    k_split_rows<<<grid, 256, 0, s>>>(x_sorted, n, hidden, x_split);
+    MOE_CHECK_LAUNCH();
+    x_in = x_split;
+  }
+  int st = launch_one<true>(a, x_in, P, narrow, s);
   if (st != MOE_OK) return st;
   a.K = inter;
   a.rows = hidden;
   a.out = y_sorted;
-  return launch_one<false>(a, h_sorted, P, s);
+  return launch_one<false>(a, h_sorted, P, narrow, s);
 }
 
 }  // namespace moe

@@ -38,7 +38,8 @@ int launch_combine_partials(const float* part, int S, const int32_t* pair_slot,
 int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
                                 const int32_t* expert_offsets, const uint16_t* x_sorted,
                                 int64_t P, int hidden, int inter, uint16_t* h_sorted,
-                                uint16_t* y_sorted, cudaStream_t s);
+                                uint16_t* y_sorted, uint16_t* x_split, cudaStream_t s);
+bool gemm_narrow(int64_t P, int E);
 
 namespace {
 
@@ -69,7 +70,13 @@ struct LayerBufs {
   int32_t* sync;       // decode path: completion counters (gate_up splits, then row groups)
   uint16_t* x_sorted;  // grouped-GEMM path
   uint16_t* y_sorted;  // grouped-GEMM path
+  uint16_t* x_split;   // grouped-GEMM path, narrow tiles: tokens as bf16 hi/lo rows
 };
+
+// The narrow grouped GEMM keeps the SwiGLU activations as bf16 hi/lo row pairs
+// (two rows per token-expert pair) and needs the tokens split the same way.
+// A call of P pairs can take narrow tiles only if P <= 32 x MOE_MAX_EXPERTS.
+bool may_be_narrow(int64_t P) { return P <= (int64_t)32 * MOE_MAX_EXPERTS; }
 
 size_t carve_layer(unsigned char* ws, int64_t T, int hidden, int inter, int E, int k,
                    LayerBufs* b) {
@@ -79,7 +86,9 @@ size_t carve_layer(unsigned char* ws, int64_t T, int hidden, int inter, int E, i
   b->pair_token = c.take<int32_t>(P);
   b->pair_weight = c.take<float>(P);
   b->pair_slot = c.take<int32_t>(P);
-  b->h_sorted = c.take<uint16_t>((size_t)P * inter);
+  const bool narrow = !use_decode_path(T) && gemm_narrow(P, E);
+  b->h_sorted = c.take<uint16_t>((size_t)(narrow ? 2 * P : P) * inter);
+  b->x_split = nullptr;
   if (use_decode_path(T)) {
     b->y_part = c.take<float>((size_t)P * decode_splits(inter) * hidden);
     b->sync = c.take<int32_t>(decode_sync_words(inter) + hidden / 16);
@@ -89,6 +98,7 @@ size_t carve_layer(unsigned char* ws, int64_t T, int hidden, int inter, int E, i
     b->sync = nullptr;
     b->x_sorted = c.take<uint16_t>((size_t)P * hidden);
     b->y_sorted = c.take<uint16_t>((size_t)P * hidden);
+    if (narrow) b->x_split = c.take<uint16_t>((size_t)2 * P * hidden);
   }
   return c.used;
 }
@@ -154,7 +164,7 @@ extern "C" int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
   st = moe_gather_rows(h, b.pair_token, P, hidden, b.x_sorted, s);
   if (st != MOE_OK) return st;
   st = launch_grouped_gemm_experts(experts, E, b.offsets, b.x_sorted, P, hidden, inter, b.h_sorted,
-                                   b.y_sorted, s);
+                                   b.y_sorted, b.x_split, s);
   if (st != MOE_OK) return st;
   return moe_combine(b.y_sorted, b.pair_slot, indices, weights, T, k, hidden, out, s);
 }
@@ -166,11 +176,14 @@ struct ExpertBufs {
   uint16_t* h;
   float* y_part;
   int32_t* sync;
+  uint16_t* x_split;
 };
 size_t carve_expert(unsigned char* ws, int64_t n, int hidden, int inter, ExpertBufs* b) {
   Carver c{ws};
   b->offsets = c.take<int32_t>(2);
-  b->h = c.take<uint16_t>((size_t)n * inter);
+  const bool narrow = !use_decode_path(n) && gemm_narrow(n, 1);
+  b->h = c.take<uint16_t>((size_t)(narrow ? 2 * n : n) * inter);
+  b->x_split = narrow ? c.take<uint16_t>((size_t)2 * n * hidden) : nullptr;
   if (use_decode_path(n)) {
     b->y_part = c.take<float>((size_t)n * decode_splits(inter) * hidden);
     b->sync = c.take<int32_t>(decode_sync_words(inter));
@@ -212,7 +225,8 @@ extern "C" int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t
     if (st != MOE_OK) return st;
     return launch_reduce_partials(b.y_part, n, decode_splits(inter), hidden, y, s);
   }
-  return launch_grouped_gemm_experts(expert, 1, b.offsets, x, n, hidden, inter, b.h, y, s);
+  return launch_grouped_gemm_experts(expert, 1, b.offsets, x, n, hidden, inter, b.h, y, b.x_split,
+                                     s);
 }
 
 // ---------------------------------------------------------------------------
@@ -224,10 +238,15 @@ struct StageBufs {
   uint16_t* h;
   float* y_part;
   int32_t* sync;
+  uint16_t* x_split;
 };
+// The expert count is not known when the workspace is sized: room for narrow
+// tiles is reserved whenever P pairs could take them.
 size_t carve_stage(unsigned char* ws, int64_t P, int hidden, int inter, StageBufs* b) {
   Carver c{ws};
-  b->h = c.take<uint16_t>((size_t)P * inter);
+  const bool split = !use_decode_path(P) && may_be_narrow(P);
+  b->h = c.take<uint16_t>((size_t)(split ? 2 * P : P) * inter);
+  b->x_split = split ? c.take<uint16_t>((size_t)2 * P * hidden) : nullptr;
   b->y_part = use_decode_path(P) ? c.take<float>((size_t)P * decode_splits(inter) * hidden) : nullptr;
   b->sync = use_decode_path(P) ? c.take<int32_t>(decode_sync_words(inter)) : nullptr;
   return c.used;
@@ -265,5 +284,5 @@ extern "C" int moe_experts_forward(const moe_nf4_expert_t* experts, int E,
     return launch_reduce_partials(b.y_part, P, decode_splits(inter), hidden, y_sorted, s);
   }
   return launch_grouped_gemm_experts(experts, E, expert_offsets, x_sorted, P, hidden, inter, b.h,
-                                     y_sorted, s);
+                                     y_sorted, b.x_split, s);
 }

@@ -74,13 +74,19 @@ class ExpertParallelMoE:
     def __call__(self, h: torch.Tensor) -> torch.Tensor:
         return self.forward(h)
 
-    def _dispatch(self, h: torch.Tensor):
+    def _exchange(self, out: torch.Tensor, inp: torch.Tensor, exchange: bool) -> None:
+        if exchange:
+            dist.all_to_all_single(out, inp, group=self.group)
+        else:  # timing aid: the kernels alone, each rank exchanging with itself
+            out.copy_(inp)
+
+    def _dispatch(self, h: torch.Tensor, exchange: bool = True):
         E, G, cap, k = self.num_experts, self.world, self.cap, self.top_k
         _, w, idx = kernels.router_topk(h, self.router.gate_f16(), k, with_logits=False)
         offsets, pair_token, _, pair_slot = kernels.permute(idx, w, E)
         send, slot_ep = kernels.ep_dispatch(h, offsets, pair_token, pair_slot, k, E, G, cap)
         recv = torch.empty_like(send)
-        dist.all_to_all_single(recv, send, group=self.group)  # rows + count headers
+        self._exchange(recv, send, exchange)  # rows + count headers
         x_sorted, local_off, recv_counts = kernels.ep_receive(recv, E, G, cap)
         return x_sorted, local_off, recv_counts, slot_ep, idx, w
 
@@ -90,17 +96,32 @@ class ExpertParallelMoE:
         x_sorted, local_off, _, _, _, _ = self._dispatch(h.contiguous())
         return x_sorted, local_off
 
+    def exchange_buffers(self, tokens: int):
+        """Buffers shaped like one call's two exchanges (for timing the all-to-alls alone)."""
+        rows_d = self.world * (self.cap + 1)
+        rows_r = self.world * self.cap
+        dev = self.router.gate_f16().device
+        return [torch.empty(r, self.hidden, dtype=torch.float16, device=dev)
+                for r in (rows_d, rows_d, rows_r, rows_r)]
+
+    def exchange_only(self, bufs) -> None:
+        """The layer's two all-to-alls on preallocated buffers, nothing else."""
+        send, recv, back, home = bufs
+        dist.all_to_all_single(recv, send, group=self.group)
+        dist.all_to_all_single(home, back, group=self.group)
+
     @torch.no_grad()
-    def forward(self, h: torch.Tensor) -> torch.Tensor:
+    def forward(self, h: torch.Tensor, exchange: bool = True) -> torch.Tensor:
+        """The layer; ``exchange=False`` (a timing aid) replaces both all-to-alls by local copies."""
         if h.ndim != 2 or h.shape[1] != self.hidden:
             raise ValueError(f"expected [tokens, {self.hidden}] fp16, got {tuple(h.shape)}")
         if h.shape[0] > self.max_tokens:
             raise ValueError(f"{h.shape[0]} tokens exceed max_tokens={self.max_tokens}")
         h = h.contiguous()
         E, G, cap = self.num_experts, self.world, self.cap
-        x_sorted, local_off, recv_counts, slot_ep, idx, w = self._dispatch(h)
+        x_sorted, local_off, recv_counts, slot_ep, idx, w = self._dispatch(h, exchange)
         y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden, self.inter)
         y_back = kernels.ep_return(y_sorted, recv_counts, E, G, cap)
         y_home = torch.empty_like(y_back)
-        dist.all_to_all_single(y_home, y_back, group=self.group)
+        self._exchange(y_home, y_back, exchange)
         return kernels.combine(y_home, slot_ep, idx, w)

@@ -199,8 +199,20 @@ class TransferScheduler:
         return TransferHandle(request_id=request.request_id, layer_id=request.layer_id,
                               expert_id=request.expert_id, slot=slot, event=event, status=status)
 
+    def _reap_cancelled(self) -> None:
+        """Free the slots of cancelled copies that have landed."""
+        for key, h in list(self._async_in_flight.items()):
+            if h.status == TransferStatus.CANCELLED and h.event.query():
+                self._staging_pool.mark_transfer_complete(h.slot, self._transfer_stream)
+                self._staging_pool.release(h.slot)
+                del self._async_in_flight[key]
+
     def submit_async(self, request: TransferRequest) -> TransferHandle:
-        """Start a CPU->GPU copy; the handle becomes READY through :meth:`poll_async`."""
+        """Start a CPU->GPU copy; the handle becomes READY through :meth:`poll_async`.
+
+        A copy of the same expert that was cancelled but is still registered
+        is revived (its bytes land regardless) instead of copied again.
+        """
         if request.direction != TransferDirection.CPU_TO_GPU:
             raise ValueError("submit_async() only supports CPU_TO_GPU transfers")
         key = (request.layer_id, request.expert_id)
@@ -208,7 +220,11 @@ class TransferScheduler:
             return self._handle(request, TransferStatus.READY)
         existing = self._async_in_flight.get(key)
         if existing is not None:
+            if existing.status == TransferStatus.CANCELLED:
+                existing.status = TransferStatus.IN_FLIGHT
             return existing
+        if self._staging_pool is not None and self._transfer_stream is not None:
+            self._reap_cancelled()
         if len(self._async_in_flight) >= self.max_concurrent:
             return self._handle(request, TransferStatus.REJECTED)
         if self._staging_pool is None or self._transfer_stream is None:
@@ -235,16 +251,19 @@ class TransferScheduler:
         return handle
 
     def adopt_async(self, layer_id: int, expert_id: int):
-        """Take over an in-flight asynchronous copy now; returns the GPU expert or ``None``.
+        """Take over an asynchronous copy now; returns the GPU expert or ``None``.
 
         The caller needs the expert before the copy has been polled complete:
         the current stream waits on the copy's event (no host wait), the expert
-        is reconstructed and cached as :meth:`poll_async` would.  ``None`` when
-        no live (non-cancelled) copy of this expert is in flight.
+        is reconstructed and cached as :meth:`poll_async` would.  A copy that
+        was cancelled but not yet reaped is taken too.  ``None`` when no copy
+        of this expert is registered.
         """
         key = (layer_id, expert_id)
         handle = self._async_in_flight.get(key)
-        if handle is None or handle.status != TransferStatus.IN_FLIGHT:
+        # A cancelled copy still lands: its bytes are as good as a new copy's.
+        if handle is None or handle.status not in (TransferStatus.IN_FLIGHT,
+                                                   TransferStatus.CANCELLED):
             return None
         torch.cuda.current_stream().wait_event(handle.event)
         try:
