@@ -508,6 +508,8 @@ def run_device(args, rank: int, world: int, local_rank: int):
         if not args.no_extra:
             line.update(measure_batches(gates, tables, dev, L, K))
             line["config0"] = measure_config0(tables, dev, K)
+            if not args.no_offload:  # the resident stack (25 GB) stays; 180 GB of HBM hold both
+                line["config3"] = measure_config3(dev)
     else:
         line["ep_parity"] = ep_par
         line["ep_breakdown"] = ep_split
@@ -646,6 +648,126 @@ def ep_parity(ep_layer0, tok, dev, rank: int):
     return {"max_abs": float(v[1]), "rel_l2": float(v[0]), "ok": bool(v[2] < 0),
             "check": "layer 0, each rank's step-0 tokens: expert-parallel vs single-GPU fused "
                      "layer with all 8 experts local; worst over ranks"}
+
+
+class SyntheticMixtral:
+    """A ModelLoader stand-in serving a seeded random-init Mixtral-8x7B.
+
+    Dense weights N(0, 0.02) fp16 on the device (norm weights 1), gate as the
+    decode workload's (same seeds), experts NF4-quantized on the device from
+    the same per-(layer, expert) seeds and handed out as CPU experts whose
+    tensors live in one pinned slab each (``pin_expert``).
+    """
+
+    def __init__(self, layers: int, device, vocab: int = 32000) -> None:
+        self.layers, self.device, self.vocab = layers, device, vocab
+
+    def load(self) -> None:
+        pass
+
+    def _randn(self, *shape, seed: int):
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        return (torch.randn(*shape, generator=g, device=self.device) * 0.02).to(torch.float16)
+
+    def load_layer(self, l: int):
+        from moeinfra_b200.model.types import LayerWeights
+        one = torch.ones(HIDDEN, dtype=torch.float16, device=self.device)
+        return LayerWeights(input_layernorm=one, q_proj=self._randn(HIDDEN, HIDDEN, seed=5 * l + 1),
+                            k_proj=self._randn(1024, HIDDEN, seed=5 * l + 2),
+                            v_proj=self._randn(1024, HIDDEN, seed=5 * l + 3),
+                            o_proj=self._randn(HIDDEN, HIDDEN, seed=5 * l + 4),
+                            post_attention_layernorm=one, moe_gate=make_gate(l, self.device))
+
+    def load_embeddings(self):
+        return self._randn(self.vocab, HIDDEN, seed=777)
+
+    def load_final_norm(self):
+        return torch.ones(HIDDEN, dtype=torch.float16, device=self.device)
+
+    def load_lm_head(self):
+        return self._randn(self.vocab, HIDDEN, seed=778)
+
+    def load_expert(self, l: int, e: int):
+        from moeinfra_b200.model.expert import PrequantizedNF4Expert
+        from moeinfra_b200.model.nf4_format import BLOB_KEY, pack_blob
+        from moeinfra_b200.transfer.reusable_staging import pin_expert
+        st = {}
+        for name, (q, a, c) in make_expert_store(l, e, self.device).items():
+            rows, cols = (FFN, HIDDEN) if name != "w2" else (HIDDEN, FFN)
+            st[name] = {"weight": q.cpu(), "weight.absmax": a.cpu(), "weight.quant_map": c.cpu(),
+                        BLOB_KEY: pack_blob({"quant_type": "nf4", "blocksize": 64,
+                                             "dtype": "bfloat16", "shape": [rows, cols]})}
+        ex = PrequantizedNF4Expert.from_serialized(st["w1"], st["w2"], st["w3"], HIDDEN, FFN)
+        pin_expert(ex)
+        return ex
+
+
+def pinned_h2d_peak_gbs(dev) -> float:
+    """Measured pinned host -> device copy bandwidth (1 GiB, best of 3)."""
+    n = 1 << 30
+    src = torch.empty(n, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(n, dtype=torch.uint8, device=dev)
+    best = 0.0
+    for _ in range(3):
+        a, b = _events()
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        best = max(best, n / (a.elapsed_time(b) / 1e3) / 1e9)
+    del src, dst
+    return best
+
+
+def measure_config3(dev):
+    """Config 3: full random-init Mixtral-8x7B, 40-token prompt -> 32 greedy tokens, bs1, offload.
+
+    ``InferenceEngine.generate`` with a 4 GiB GPU expert cache (43 Mixtral
+    experts, LRU), every expert in the CPU tier in pinned memory; each miss is
+    one H2D copy on the copy stream.  One warm-up generation, then one timed.
+    """
+    from moeinfra_b200.engine.engine import InferenceEngine
+    from moeinfra_b200.engine.types import ForwardRequest
+    from moeinfra_b200.transfer.scheduler import EXECUTE_NEXT_PROFILE
+    budget = 4 << 30
+    slots = budget // EXPERT_BYTES
+    cfg = {"model": {"name": None, "num_layers": LAYERS, "num_experts": EXPERTS,
+                     "num_experts_per_tok": TOP_K, "hidden_size": HIDDEN, "intermediate_size": FFN,
+                     "num_attention_heads": 32, "num_key_value_heads": 8, "vocab_size": 32000,
+                     "rope_theta": 1e6, "rms_norm_eps": 1e-5, "device": str(dev)},
+           "cache": {"gpu_slots": int(slots), "cpu_slots": LAYERS * EXPERTS,
+                     "eviction_policy": "lru", "gpu_budget_bytes": budget},
+           "transfer": {"bandwidth_gbps": 50.0, "max_concurrent_transfers": 2},
+           "engine": {"max_batch": 1, "max_seq_len": 128}}
+    loader = SyntheticMixtral(LAYERS, dev)
+    t0 = time.perf_counter()
+    eng = InferenceEngine(cfg, model_loader=loader)
+    for l in range(LAYERS):
+        for e in range(EXPERTS):
+            eng.cache_manager.put(l, e, loader.load_expert(l, e), device="cpu")
+    setup_s = time.perf_counter() - t0
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, 32000, (1, 40), generator=g)
+    eng.generate(ForwardRequest(input_ids=prompt, max_new_tokens=32))  # warm-up
+    n0 = len(EXECUTE_NEXT_PROFILE)
+    res = eng.generate(ForwardRequest(input_ids=torch.randint(0, 32000, (1, 40), generator=g),
+                                      max_new_tokens=32))
+    prof = EXECUTE_NEXT_PROFILE[n0:]
+    h2d = sum(p.get("bytes_transferred", 0) for p in prof)
+    total_s = (res.ttft_ms + res.stage_timings["decode"]) / 1e3
+    peak = pinned_h2d_peak_gbs(dev)
+    gbs = h2d / total_s / 1e9
+    eng.close()
+    del eng
+    torch.cuda.empty_cache()
+    return {"value": round(res.tps, 3), "unit": "tok/s (decode, bs1)",
+            "ttft_ms": round(res.ttft_ms, 1), "decode_ms": round(res.stage_timings["decode"], 1),
+            "experts_moved": len(prof), "h2d_bytes": int(h2d),
+            "h2d_gbs": round(gbs, 2), "pinned_h2d_peak_gbs": round(peak, 2),
+            "host_link_frac": round(gbs / peak, 4), "gpu_expert_slots": int(slots),
+            "setup_s": round(setup_s, 1),
+            "note": "InferenceEngine.generate, 32-layer random-init Mixtral-8x7B, 40 random ids -> "
+                    "32 greedy tokens, 4 GiB GPU expert cache (LRU), pinned CPU tier, eager decode"}
 
 
 def measure_config0(tables, dev, K: int):
@@ -818,7 +940,9 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
-                    help="skip the bs64 and prefill measurements")
+                    help="skip the bs64, prefill, config-0 and config-3 measurements")
+    ap.add_argument("--no-offload", action="store_true",
+                    help="skip the config-3 (full model, CPU-offloaded experts) measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

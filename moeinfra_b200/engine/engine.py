@@ -83,7 +83,11 @@ def expert_bytes(hidden: int, inter: int) -> int:
 class InferenceEngine:
     """Mixtral NF4 MoE inference with GPU-resident or CPU-offloaded experts."""
 
-    def __init__(self, config: dict, logger: Optional[logging.Logger] = None) -> None:
+    def __init__(self, config: dict, logger: Optional[logging.Logger] = None,
+                 model_loader=None) -> None:
+        """``model_loader`` (optional) replaces the ``ModelLoader`` built from ``model.name``:
+        any object with the loader's ``load`` / ``load_layer`` / ``load_embeddings`` /
+        ``load_final_norm`` / ``load_lm_head`` / ``load_expert`` methods."""
         self.config = config
         self._logger = logger or logging.getLogger(__name__)
         model_cfg = config.get("model", {})
@@ -127,7 +131,7 @@ class InferenceEngine:
             cache_manager=self._cache_manager, transfer_scheduler=self._transfer_scheduler,
             policy=PrefetchPolicy(transfer_cfg.get("prefetch_policy", "none")),
             depth=transfer_cfg.get("prefetch_depth", 2), logger=self._logger)
-        self._model = ModelLoader(
+        self._model = model_loader if model_loader is not None else ModelLoader(
             model_name=model_cfg.get("name"), num_layers=self._num_layers,
             num_experts=self._num_experts, hidden_size=self._hidden,
             intermediate_size=self._inter, quantization=model_cfg.get("quantization", "int4"),

@@ -30,3 +30,20 @@ def transfer_staged_expert_to_gpu(slot: StagingSlot, stream: torch.cuda.Stream,
     # recycling it until that stream's work is done as well.
     dev.record_stream(torch.cuda.current_stream(device))
     return slab_views(dev, slot.layout)
+
+
+def transfer_pinned_expert_to_gpu(expert, stream: torch.cuda.Stream,
+                                  device: torch.device | str | None = None) -> dict:
+    """One H2D copy of an expert whose CPU copy lives in a pinned slab (``pin_expert``)."""
+    slab = getattr(expert, "pinned_slab", None)
+    if slab is None:
+        raise RuntimeError("expert has no pinned slab; stage it through a staging slot")
+    device = torch.device(device) if device is not None else torch.device(
+        "cuda", torch.cuda.current_device())
+    nbytes = expert.pinned_bytes
+    with torch.cuda.stream(stream):
+        dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        dev.copy_(slab[:nbytes], non_blocking=True)
+    dev.record_stream(torch.cuda.current_stream(device))
+    return slab_views(dev, expert.pinned_layout)
+

@@ -207,3 +207,47 @@ class ReusablePinnedStagingPool:
             raise ValueError("Existing staging buffer does not match source tensor")
         existing.copy_(source)
         return existing
+
+
+def pin_expert(expert) -> int:
+    """Move a CPU expert's NF4 tensors into ONE page-locked slab, in place.
+
+    The CPU tier is authoritative and, where host RAM allows, can live in
+    pinned memory: a GPU miss is then a single ``cudaMemcpyAsync`` of the slab
+    (no pageable -> pinned staging copy of ~95 MB per Mixtral expert).  The
+    expert's serialized tensors are rebound to views of the slab (no second
+    copy is kept); ``expert.pinned_slab`` / ``pinned_layout`` /
+    ``pinned_bytes`` describe it for :func:`~moeinfra_b200.transfer.nf4_transfer.transfer_pinned_expert_to_gpu`.
+    Returns the slab size in bytes.
+    """
+    if getattr(expert, "pinned_slab", None) is not None:
+        return expert.pinned_bytes
+    states = {n: ReusablePinnedStagingPool._projection_state(expert, n)
+              for n in ReusablePinnedStagingPool._PROJECTIONS}
+    layout, nbytes = plan_layout(states)
+    slab = torch.empty(max(nbytes, 1), dtype=torch.uint8, pin_memory=_pin_available())
+    views = slab_views(slab, layout)
+    for proj, key, off, shape, dtype in layout:
+        if off is not None:
+            views[proj][key].copy_(states[proj][key].detach().reshape(shape))
+    # Rebind the serialized entries that the canonical keys came from.
+    rename = {"absmax": "weight.absmax", "code": "weight.quant_map",
+              "state2_absmax": "weight.nested_absmax", "state2_code": "weight.nested_quant_map"}
+    for proj in ReusablePinnedStagingPool._PROJECTIONS:
+        raw = getattr(expert, proj)
+        raw = raw if isinstance(raw, dict) else getattr(raw, "state", None)
+        if not isinstance(raw, dict):
+            continue
+        for key, view in views[proj].items():
+            if view is None:
+                continue
+            for name in (key, rename.get(key)):
+                if name in raw and isinstance(raw[name], torch.Tensor) and \
+                        raw[name].numel() == view.numel() and raw[name].dtype == view.dtype:
+                    raw[name] = view.reshape(raw[name].shape)
+                    break
+    expert.pinned_slab = slab
+    expert.pinned_layout = layout
+    expert.pinned_bytes = nbytes
+    return nbytes
+

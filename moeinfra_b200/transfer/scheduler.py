@@ -25,7 +25,9 @@ import torch
 
 from moeinfra_b200.transfer.bandwidth import BandwidthMonitor
 from moeinfra_b200.transfer.nf4_reconstruct import ReconstructedNF4Expert
-from moeinfra_b200.transfer.nf4_transfer import transfer_staged_expert_to_gpu
+from moeinfra_b200.transfer.nf4_transfer import (
+    transfer_pinned_expert_to_gpu, transfer_staged_expert_to_gpu,
+)
 from moeinfra_b200.transfer.types import (
     TransferDirection, TransferHandle, TransferRequest, TransferResult, TransferStatus,
 )
@@ -85,8 +87,26 @@ class TransferScheduler:
         return self._bw_monitor
 
     # -- synchronous-API execution ------------------------------------------
+    def _copy_pinned(self, cpu_expert, profile: dict):
+        """The CPU copy already lives in a pinned slab: one H2D copy, no staging."""
+        start = torch.cuda.Event(enable_timing=True) if self.synchronous else None
+        if start is not None:
+            start.record(self._transfer_stream)
+        profile["staging_ms"] = 0.0
+        gpu_state = transfer_pinned_expert_to_gpu(cpu_expert, self._transfer_stream)
+        done = torch.cuda.Event(enable_timing=self.synchronous)
+        done.record(self._transfer_stream)
+        if self.synchronous:
+            self._transfer_stream.synchronize()
+            profile["h2d_cuda_ms"] = start.elapsed_time(done)
+        else:
+            torch.cuda.current_stream().wait_event(done)
+        return gpu_state
+
     def _stage_and_copy(self, cpu_expert, request: TransferRequest, profile: dict):
-        """Stage into a pinned slab, one H2D copy; returns (gpu_state, slot, done_event)."""
+        """Stage into a pinned slab, one H2D copy; returns the device state."""
+        if getattr(cpu_expert, "pinned_slab", None) is not None:
+            return self._copy_pinned(cpu_expert, profile)
         slot = self._staging_pool.acquire(wait=True)
         if slot is None:
             raise RuntimeError("No staging slot available for synchronous transfer")
@@ -199,12 +219,17 @@ class TransferScheduler:
         return TransferHandle(request_id=request.request_id, layer_id=request.layer_id,
                               expert_id=request.expert_id, slot=slot, event=event, status=status)
 
+    def _release_slot(self, slot) -> None:
+        """Hand a staging slot back once its copy (queued on the copy stream) is done."""
+        if slot is not None:
+            self._staging_pool.mark_transfer_complete(slot, self._transfer_stream)
+            self._staging_pool.release(slot)
+
     def _reap_cancelled(self) -> None:
         """Free the slots of cancelled copies that have landed."""
         for key, h in list(self._async_in_flight.items()):
             if h.status == TransferStatus.CANCELLED and h.event.query():
-                self._staging_pool.mark_transfer_complete(h.slot, self._transfer_stream)
-                self._staging_pool.release(h.slot)
+                self._release_slot(h.slot)
                 del self._async_in_flight[key]
 
     def submit_async(self, request: TransferRequest) -> TransferHandle:
@@ -229,21 +254,26 @@ class TransferScheduler:
             return self._handle(request, TransferStatus.REJECTED)
         if self._staging_pool is None or self._transfer_stream is None:
             raise RuntimeError("Async transfer requires staging_pool and transfer_stream")
-        slot = self._staging_pool.acquire()
-        if slot is None:
-            return self._handle(request, TransferStatus.REJECTED)
         expert = self._cache_manager.peek_cpu(*key)
         if expert is None:
-            self._staging_pool.release(slot)
             return self._handle(request, TransferStatus.REJECTED)
-        try:
-            self._staging_pool.stage_expert(slot, expert, *key)
-            gpu_state = transfer_staged_expert_to_gpu(slot, self._transfer_stream)
+        slot = None
+        if getattr(expert, "pinned_slab", None) is not None:
+            gpu_state = transfer_pinned_expert_to_gpu(expert, self._transfer_stream)
             event = torch.cuda.Event()
             event.record(self._transfer_stream)
-        except Exception:
-            self._staging_pool.release(slot)
-            raise
+        else:
+            slot = self._staging_pool.acquire()
+            if slot is None:
+                return self._handle(request, TransferStatus.REJECTED)
+            try:
+                self._staging_pool.stage_expert(slot, expert, *key)
+                gpu_state = transfer_staged_expert_to_gpu(slot, self._transfer_stream)
+                event = torch.cuda.Event()
+                event.record(self._transfer_stream)
+            except Exception:
+                self._staging_pool.release(slot)
+                raise
         handle = self._handle(request, TransferStatus.IN_FLIGHT, slot=slot, event=event)
         handle.gpu_state = gpu_state
         handle.cpu_expert = expert
@@ -274,8 +304,7 @@ class TransferScheduler:
             self._bw_monitor.record(self._cache_manager.get_size_bytes(layer_id, expert_id))
             return expert
         finally:
-            self._staging_pool.mark_transfer_complete(handle.slot, self._transfer_stream)
-            self._staging_pool.release(handle.slot)
+            self._release_slot(handle.slot)
             del self._async_in_flight[key]
 
     def poll_async(self, layer_id: int, expert_id: int) -> TransferStatus:
@@ -287,8 +316,7 @@ class TransferScheduler:
         if handle.status == TransferStatus.CANCELLED:
             if not done:
                 return TransferStatus.CANCELLED
-            self._staging_pool.mark_transfer_complete(handle.slot, self._transfer_stream)
-            self._staging_pool.release(handle.slot)
+            self._release_slot(handle.slot)
             del self._async_in_flight[key]
             return TransferStatus.CANCELLED
         if not done:
@@ -297,12 +325,12 @@ class TransferScheduler:
             expert = ReconstructedNF4Expert(handle.cpu_expert, handle.gpu_state)
             self._cache_manager.put(layer_id, expert_id, expert, device="cuda")
             handle.status = TransferStatus.READY
-            self._staging_pool.mark_transfer_complete(handle.slot, self._transfer_stream)
-            self._staging_pool.release(handle.slot)
+            self._release_slot(handle.slot)
             del self._async_in_flight[key]
             return TransferStatus.READY
         except Exception:
             handle.status = TransferStatus.REJECTED
-            self._staging_pool.release(handle.slot)
+            if handle.slot is not None:
+                self._staging_pool.release(handle.slot)
             del self._async_in_flight[key]
             raise

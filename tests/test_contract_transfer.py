@@ -373,3 +373,24 @@ def test_stage_expert_refuses_an_expert_larger_than_the_slot():
     slot = pool.acquire()
     with pytest.raises(ValueError, match="staging bytes"):
         pool.stage_expert(slot, _expert_states(False), 0, 0)
+
+
+@pytest.mark.parametrize("nested", [False, True])
+def test_pin_expert_packs_one_slab_and_rebinds_the_tensors(nested):
+    from moeinfra_b200.model.nf4_format import canonical_state
+    from moeinfra_b200.transfer.reusable_staging import pin_expert, slab_views
+
+    ex = _expert_states(nested)
+    want = {p: {k: (None if v is None else v.clone()) for k, v in
+                canonical_state(getattr(ex, p), p).items()} for p in ("w1", "w2", "w3")}
+    nbytes = pin_expert(ex)
+    assert nbytes == ex.pinned_bytes and pin_expert(ex) == nbytes  # idempotent
+    views = slab_views(ex.pinned_slab, ex.pinned_layout)
+    for p in ("w1", "w2", "w3"):
+        for k, t in want[p].items():
+            if t is not None:
+                assert torch.equal(views[p][k], t), (p, k)
+        # the expert's own tensors now alias the slab: no second host copy
+        w = getattr(ex, p)["weight"]
+        base = ex.pinned_slab.data_ptr()
+        assert base <= w.data_ptr() < base + ex.pinned_slab.numel()

@@ -180,3 +180,26 @@ def test_offload_at_the_mixtral_shape(tmp_path):
         want, _ = _oracle_layer(h, gate, experts, H, I)
         assert_close_fp16(out.cpu().numpy(), want, what=f"Mixtral offload T={T}")
     assert cache.stats().gpu_slots_used <= 2
+
+
+def test_pinned_cpu_tier_copies_without_staging(tmp_path):
+    """CPU experts kept in one pinned slab each: a miss is one H2D copy, no staging slot."""
+    from moeinfra_b200.transfer.reusable_staging import pin_expert
+    from moeinfra_b200.transfer.scheduler import EXECUTE_NEXT_PROFILE
+
+    H, I, E = 256, 512, 8
+    layer, cache, sched, experts, gate = _stack(tmp_path, H, I, E, gpu_slots=2, seed=21)
+    for e in range(E):
+        ex = layer.model_loader.load_expert(0, e)
+        pin_expert(ex)
+        cache.put(0, e, ex, device="cpu")
+    n0 = len(EXECUTE_NEXT_PROFILE)
+    h = torch.randn(9, H, generator=torch.Generator(device="cuda").manual_seed(3),
+                    device="cuda").half()
+    out = layer.forward(h)
+    torch.cuda.synchronize()
+    want, _ = _oracle_layer(h, gate, experts, H, I)
+    assert_close_fp16(out.cpu().numpy(), want, what="pinned CPU tier")
+    prof = EXECUTE_NEXT_PROFILE[n0:]
+    assert prof and all(p["success"] and p["staging_ms"] == 0.0 for p in prof)
+    assert sched._staging_pool.slot_count == 0  # no staging slot was ever needed
