@@ -313,16 +313,21 @@ def run_device(args, rank: int, world: int, local_rank: int):
                 [cm.peek_gpu(l, e).nf4_descriptor for e in range(EXPERTS)]))
         step_fn = None
     else:
-        from moeinfra_b200.ep import ExpertParallelMoE
+        from moeinfra_b200.ep import ExpertParallelMoE, capacity
+        from moeinfra_b200.ep_p2p import PeerExchange
         per = EXPERTS // world
         owned = list(range(rank * per, (rank + 1) * per))
-        ep_layers = []
+        peer = None
+        if args.ep_exchange == "p2p":
+            peer = PeerExchange(L, world, rank, capacity(B, TOP_K, EXPERTS, world), HIDDEN)
+        ep_layers, nccl_layers = [], []
         for l in range(L):
-            gate = make_gate(l, dev)
+            router = ExpertRouter(make_gate(l, dev), num_experts_per_tok=TOP_K)
             local = [resident_expert(l, e, dev) for e in owned]
-            ep_layers.append(ExpertParallelMoE(ExpertRouter(gate, num_experts_per_tok=TOP_K),
-                                               local, rank=rank, world_size=world,
-                                               max_tokens=B))
+            ep_layers.append(ExpertParallelMoE(router, local, rank=rank, world_size=world,
+                                               max_tokens=B, peer=peer, layer_slot=l))
+            nccl_layers.append(ExpertParallelMoE(router, local, rank=rank, world_size=world,
+                                                 max_tokens=B))
         step_fn = ep_layers
         owned_experts = owned
     torch.cuda.synchronize()
@@ -459,7 +464,7 @@ def run_device(args, rank: int, world: int, local_rank: int):
         roof = ep_roofline(step_fn, tokens[W], dev, L, K)
         e2e = ep_e2e(step_fn, tokens, dev, L, K, W, world)
         ep_par = ep_parity(step_fn[0], tokens[0], dev, rank)
-        ep_split = ep_breakdown(step_fn, tokens[W], dev, L, K, world)
+        ep_split = ep_breakdown(step_fn, nccl_layers, tokens[W], dev, L, K, world)
 
     # --- end to end through the public API, host buffers -----------------------------
     if world == 1:
@@ -525,6 +530,10 @@ def run_device(args, rank: int, world: int, local_rank: int):
     if graph is not None:
         graph.reset()  # a graph holding NCCL calls must go before the process group
         del graph
+    if world > 1 and peer is not None:
+        torch.cuda.synchronize()
+        _barrier(world)
+        peer.close()
     return line
 
 
@@ -565,26 +574,31 @@ def ep_roofline(ep_layers, tok, dev, L: int, K: int):
             "peak_source": peak[1]}
 
 
-def ep_breakdown(ep_layers, tok, dev, L: int, K: int, world: int):
+def ep_breakdown(ep_layers, nccl_layers, tok, dev, L: int, K: int, world: int):
     """Where an expert-parallel layer's time goes, each variant a CUDA graph of L layers.
 
-    full: the step as timed; kernels: the same kernels with both all-to-alls
-    replaced by local copies; a2a: the two NCCL all-to-alls per layer alone on
-    buffers of the same shapes.  Per layer, max over ranks.
+    layer: the step as timed (peer-memory exchange unless --ep-exchange nccl);
+    layer_nccl: the same layers exchanging through NCCL all-to-alls; kernels:
+    the kernels with both exchanges replaced by local copies; a2a: the two
+    NCCL all-to-alls per layer alone on buffers of the same shapes.  Per
+    layer, max over ranks.
     """
     reps = max(3, K // 2)
     h = tok.contiguous()
-    bufs = [lay.exchange_buffers(h.shape[0]) for lay in ep_layers]
+    bufs = [lay.exchange_buffers(h.shape[0]) for lay in nccl_layers]
     out = {}
     for name, fn in (
             ("layer_us", lambda: [lay.forward(h) for lay in ep_layers]),
+            ("layer_nccl_us", lambda: [lay.forward(h) for lay in nccl_layers]),
             ("kernels_only_us", lambda: [lay.forward(h, exchange=False) for lay in ep_layers]),
-            ("a2a_only_us", lambda: [lay.exchange_only(b) for lay, b in zip(ep_layers, bufs)])):
+            ("a2a_only_us", lambda: [lay.exchange_only(b) for lay, b in zip(nccl_layers, bufs)])):
         _barrier(world)
         ms = _graph_time(fn, reps, dev) / L
         out[name] = round(_max_over_ranks(ms, world, dev) * 1e3, 2)
-    out["note"] = ("per layer, CUDA graphs of the 32-layer step; kernels_only replaces the two "
-                   "NCCL all-to-alls by local copies, a2a_only runs just the two all-to-alls")
+    out["note"] = ("per layer, CUDA graphs of the 32-layer step; layer uses the peer-memory "
+                   "exchange (NVLink stores, flag waits), layer_nccl the NCCL all-to-alls; "
+                   "kernels_only replaces both exchanges by local copies, a2a_only runs just the "
+                   "two NCCL all-to-alls")
     return out
 
 
@@ -941,6 +955,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the bs64, prefill, config-0 and config-3 measurements")
+    ap.add_argument("--ep-exchange", choices=("p2p", "nccl"), default="p2p",
+                    help="expert-parallel token exchange: stores into peer memory, or NCCL")
     ap.add_argument("--no-offload", action="store_true",
                     help="skip the config-3 (full model, CPU-offloaded experts) measurement")
     args = ap.parse_args()

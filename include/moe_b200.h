@@ -316,6 +316,38 @@ int moe_ep_receive(const uint16_t* recv_rows, int32_t* recv_counts, int E,
 int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_counts, int E,
                   int G, int cap, int hidden, uint16_t* y_back, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Expert-parallel exchange over peer memory (NVLink), in place of the two
+ * all-to-alls.  No counterpart in the reference (single-GPU).  Each rank owns,
+ * per exchange, a receive region laid out as the all-to-all would deliver it
+ * (G chunks, chunk s from source rank s) and an int32 flag per source, both
+ * mapped into every peer (e.g. CUDA IPC); peer_* are device arrays [G] of
+ * those addresses (uint64).  seq and done are this rank's own device ints
+ * for the exchange (both start at 0; done returns to 0 after every call).
+ *
+ * moe_ep_dispatch_p2p: moe_ep_dispatch that stores chunk r (cap rows + the
+ *   count header row, cap + 1 rows) straight into rank r's receive region at
+ *   chunk `rank`; when every CTA has stored, the launch bumps *seq and
+ *   release-stores it into flag `rank` of every peer.
+ * moe_ep_wait_p2p: bounded wait until all G of this rank's flags reach its
+ *   *seq (the value its own send of the same exchange produced); then
+ *   moe_ep_receive / moe_combine read the region with the ordinary kernels.
+ *   A wait that runs out sets error bit 1 (moe_stream_check: MOE_ERR_TIMEOUT).
+ * moe_ep_return_p2p: moe_ep_return that stores the rows for source s straight
+ *   into s's return region (G chunks of cap rows) at chunk `rank`, then
+ *   signals like the dispatch.
+ * Calls of one exchange must not overlap; give every layer its own regions.
+ */
+int moe_ep_dispatch_p2p(const uint16_t* h, const int32_t* expert_offsets,
+                        const int32_t* pair_token, const int32_t* pair_slot, int64_t T,
+                        int k, int E, int G, int rank, int cap, int hidden,
+                        const uint64_t* peer_recv, const uint64_t* peer_flags,
+                        int32_t* seq, int32_t* done, int32_t* pair_slot_ep, void* stream);
+int moe_ep_return_p2p(const uint16_t* y_sorted, const int32_t* recv_counts, int E, int G,
+                      int rank, int cap, int hidden, const uint64_t* peer_back,
+                      const uint64_t* peer_flags, int32_t* seq, int32_t* done, void* stream);
+int moe_ep_wait_p2p(const int32_t* flags, int G, const int32_t* seq, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

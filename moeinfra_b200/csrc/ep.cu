@@ -145,6 +145,118 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_move(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Exchange over peer memory (NVLink), no collective library.  Every rank owns,
+// per exchange, a receive region of G chunks (one per source rank, the layout
+// the all-to-all would deliver) and G flags, mapped into its peers' address
+// spaces.  A sender stores its chunk for rank r straight into r's region at
+// chunk `rank`; when every CTA of the launch has stored (system-scope fence,
+// then a CTA completion count), the last CTA bumps this exchange's local
+// sequence number and release-stores it into flag `rank` of every peer.  The
+// receiver waits (bounded) until all G flags reach its own sequence number
+// (each rank sends once and receives once per exchange, so the numbers agree)
+// and then reads its region with the ordinary receive / combine kernels.
+
+MOE_DEFINE_ERROR_WORD()
+
+__device__ __forceinline__ void signal_peers(const uint64_t* __restrict__ peer_flags, int G,
+                                             int rank, int32_t* seq, int32_t* done) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(done, 1) == static_cast<int>(gridDim.x) - 1) {
+      __threadfence_system();
+      const int s = *reinterpret_cast<volatile int32_t*>(seq) + 1;
+      *reinterpret_cast<volatile int32_t*>(seq) = s;
+      for (int r = 0; r < G; ++r) {
+        int32_t* f = reinterpret_cast<int32_t*>(peer_flags[r]) + rank;
+        asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f), "r"(s) : "memory");
+      }
+      *reinterpret_cast<volatile int32_t*>(done) = 0;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kEpThreads) k_ep_dispatch_p2p(
+    const uint4* __restrict__ h, const int32_t* __restrict__ offsets,
+    const int32_t* __restrict__ pair_token, const int32_t* __restrict__ pair_slot, int64_t P,
+    int E, int El, int G, int rank, int cap, int vpr, const uint64_t* __restrict__ peer_recv,
+    const uint64_t* __restrict__ peer_flags, int32_t* seq, int32_t* done,
+    int32_t* __restrict__ pair_slot_ep) {
+  __shared__ int s_off[kEpMaxExperts + 1];
+  if (threadIdx.x <= E) s_off[threadIdx.x] = offsets[threadIdx.x];
+  __syncthreads();
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t chunk = (int64_t)(cap + 1) * vpr;  // one source's chunk in a receive region
+  if (tid < E) {  // header row of the chunk for rank r: r's expert counts from this rank
+    const int r = static_cast<int>(tid) / El, j = static_cast<int>(tid) - r * El;
+    uint4* dst = reinterpret_cast<uint4*>(peer_recv[r]) + rank * chunk + (int64_t)cap * vpr;
+    reinterpret_cast<int32_t*>(dst)[j] = s_off[tid + 1] - s_off[tid];
+  }
+  for (int64_t q = tid; q < P; q += stride) {
+    const int p = pair_slot[q];
+    int e = 0;
+    while (e + 1 < E && s_off[e + 1] <= p) ++e;
+    const int r = e / El;
+    pair_slot_ep[q] = r * cap + (p - s_off[r * El]);
+  }
+  const int64_t total = (int64_t)G * cap * vpr;
+  for (int64_t v = tid; v < total; v += stride) {
+    const int64_t row = v / vpr;
+    const int c = static_cast<int>(v - row * vpr);
+    const int r = static_cast<int>(row / cap), i = static_cast<int>(row - (int64_t)r * cap);
+    const int p = s_off[r * El] + i;
+    if (p < s_off[(r + 1) * El]) {
+      uint4* dst = reinterpret_cast<uint4*>(peer_recv[r]) + rank * chunk + (int64_t)i * vpr;
+      dst[c] = h[(int64_t)pair_token[p] * vpr + c];
+    }
+  }
+  signal_peers(peer_flags, G, rank, seq, done);
+}
+
+// Owner side of the return: y rows of source s go to s's return region, chunk
+// `rank`, at the row the source's combine expects (pair_slot_ep layout).
+__global__ void __launch_bounds__(kEpThreads) k_ep_return_p2p(
+    const uint4* __restrict__ y_sorted, const int32_t* __restrict__ counts, int El, int G,
+    int rank, int cap, int vpr, const uint64_t* __restrict__ peer_back,
+    const uint64_t* __restrict__ peer_flags, int32_t* seq, int32_t* done) {
+  __shared__ RecvPlan pl;
+  build_plan(counts, El, El, G, cap, pl);
+  const int64_t total = (int64_t)G * cap * vpr;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = v / vpr;
+    const int c = static_cast<int>(v - row * vpr);
+    const int s = static_cast<int>(row / cap), i = static_cast<int>(row - (int64_t)s * cap);
+    const int64_t src = recv_dst(pl, El, s, i);
+    if (src < 0 || src >= (int64_t)G * cap) continue;
+    uint4* dst = reinterpret_cast<uint4*>(peer_back[s]) + ((int64_t)rank * cap + i) * vpr;
+    dst[c] = y_sorted[src * vpr + c];
+  }
+  signal_peers(peer_flags, G, rank, seq, done);
+}
+
+// Bounded wait until every source's flag reaches this rank's sequence number.
+__global__ void k_ep_wait(const int32_t* flags, int G, const int32_t* seq, uint64_t limit_ns) {
+  const int s = threadIdx.x;
+  if (s >= G) return;
+  const int target = *reinterpret_cast<const volatile int32_t*>(seq);
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
+  if (v >= target) return;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    __nanosleep(200);
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
+    if (v >= target) return;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      set_device_error(kErrWaitTimeout);
+      return;
+    }
+  }
+}
+
 // The header row must hold E/G int32 counts: hidden * 2 >= 4 * E / G.
 bool ep_args_ok(int E, int G, int cap, int hidden) {
   return G >= 1 && E >= G && E <= kEpMaxExperts && E % G == 0 && cap >= 1 && hidden > 0 &&
@@ -204,3 +316,53 @@ extern "C" int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_count
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
+
+extern "C" int moe_ep_dispatch_p2p(const uint16_t* h, const int32_t* expert_offsets,
+                                   const int32_t* pair_token, const int32_t* pair_slot, int64_t T,
+                                   int k, int E, int G, int rank, int cap, int hidden,
+                                   const uint64_t* peer_recv, const uint64_t* peer_flags,
+                                   int32_t* seq, int32_t* done, int32_t* pair_slot_ep,
+                                   void* stream) {
+  using namespace moe;
+  if (T < 0 || k < 1 || !ep_args_ok(E, G, cap, hidden) || rank < 0 || rank >= G)
+    return MOE_ERR_INVALID_ARG;
+  const int El = E / G;
+  if (T * (k < El ? k : El) > cap) return MOE_ERR_INVALID_ARG;
+  if (!expert_offsets || !peer_recv || !peer_flags || !seq || !done) return MOE_ERR_INVALID_ARG;
+  if (T > 0 && (!h || !pair_token || !pair_slot || !pair_slot_ep)) return MOE_ERR_INVALID_ARG;
+  if (T > 0 && !aligned16(h)) return MOE_ERR_ALIGNMENT;
+  const int vpr = hidden / 8;
+  k_ep_dispatch_p2p<<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                      static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(h), expert_offsets, pair_token, pair_slot, T * k, E, El, G,
+      rank, cap, vpr, peer_recv, peer_flags, seq, done, pair_slot_ep);
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_return_p2p(const uint16_t* y_sorted, const int32_t* recv_counts, int E,
+                                 int G, int rank, int cap, int hidden, const uint64_t* peer_back,
+                                 const uint64_t* peer_flags, int32_t* seq, int32_t* done,
+                                 void* stream) {
+  using namespace moe;
+  if (!ep_args_ok(E, G, cap, hidden) || rank < 0 || rank >= G) return MOE_ERR_INVALID_ARG;
+  if (!y_sorted || !recv_counts || !peer_back || !peer_flags || !seq || !done)
+    return MOE_ERR_INVALID_ARG;
+  if (!aligned16(y_sorted)) return MOE_ERR_ALIGNMENT;
+  const int vpr = hidden / 8;
+  k_ep_return_p2p<<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                    static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(y_sorted), recv_counts, E / G, G, rank, cap, vpr, peer_back,
+      peer_flags, seq, done);
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_wait_p2p(const int32_t* flags, int G, const int32_t* seq, void* stream) {
+  using namespace moe;
+  if (!flags || !seq || G < 1 || G > kEpMaxExperts) return MOE_ERR_INVALID_ARG;
+  k_ep_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, G, seq, wait_limit_ns());
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+

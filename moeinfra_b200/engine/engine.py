@@ -155,9 +155,11 @@ class InferenceEngine:
             router = ExpertRouter(w.moe_gate.to(device=dev, dtype=self._dtype),
                                   num_experts_per_tok=self._num_experts_per_tok,
                                   logger=self._logger)
-            self._moe_layers.append(MoELayer(layer_id, router, self._cache_manager, self._model,
-                                             self._transfer_scheduler, logger=self._logger,
-                                             prefetch_engine=self._prefetch_engine))
+            moe = MoELayer(layer_id, router, self._cache_manager, self._model,
+                           self._transfer_scheduler, logger=self._logger,
+                           prefetch_engine=self._prefetch_engine)
+            moe.check_each_call = False  # generate() checks the device once per generation
+            self._moe_layers.append(moe)
             layers.append(w)
         self._stack = DenseStack(
             DenseConfig.from_mixtral(self._mixtral_config), layers,

@@ -55,7 +55,10 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, router, experts: Sequence, rank: int, world_size: int, max_tokens: int,
-                 group=None) -> None:
+                 group=None, peer=None, layer_slot: int = 0) -> None:
+        """``peer`` (a :class:`~moeinfra_b200.ep_p2p.PeerExchange`, optional) switches both
+        exchanges from NCCL all-to-alls to stores into peer memory; ``layer_slot`` picks this
+        layer's regions in it.  Calls with more than ``max_tokens`` tokens are refused."""
         self.router = router
         self.num_experts = router.num_experts
         self.top_k = router.num_experts_per_tok
@@ -70,6 +73,9 @@ class ExpertParallelMoE:
         self.hidden = experts[0].hidden_size
         self.inter = experts[0].intermediate_size
         self._table = kernels.expert_array([ex.nf4_descriptor for ex in self.experts])
+        self.peer, self.layer_slot = peer, layer_slot
+        if peer is not None and (peer.cap < self.cap or peer.world != world_size):
+            raise ValueError("peer exchange regions are smaller than this layer's exchange")
 
     def __call__(self, h: torch.Tensor) -> torch.Tensor:
         return self.forward(h)
@@ -118,6 +124,8 @@ class ExpertParallelMoE:
         if h.shape[0] > self.max_tokens:
             raise ValueError(f"{h.shape[0]} tokens exceed max_tokens={self.max_tokens}")
         h = h.contiguous()
+        if self.peer is not None and exchange:
+            return self._forward_p2p(h)
         E, G, cap = self.num_experts, self.world, self.cap
         x_sorted, local_off, recv_counts, slot_ep, idx, w = self._dispatch(h, exchange)
         y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden, self.inter)
@@ -125,3 +133,21 @@ class ExpertParallelMoE:
         y_home = torch.empty_like(y_back)
         self._exchange(y_home, y_back, exchange)
         return kernels.combine(y_home, slot_ep, idx, w)
+
+    def _forward_p2p(self, h: torch.Tensor) -> torch.Tensor:
+        """The layer with both exchanges as stores into peer memory (no NCCL call)."""
+        E, G, k, pe, l = self.num_experts, self.world, self.top_k, self.peer, self.layer_slot
+        cap = pe.cap
+        _, w, idx = kernels.router_topk(h, self.router.gate_f16(), k, with_logits=False)
+        offsets, pair_token, _, pair_slot = kernels.permute(idx, w, E)
+        slot_ep = kernels.ep_dispatch_p2p(h, offsets, pair_token, pair_slot, k, E, G, self.rank,
+                                          cap, pe.peer_table(l, 0), pe.peer_table(l, 2),
+                                          pe.seq(l, 0), pe.done(l, 0))
+        kernels.ep_wait_p2p(pe.own_flags(l, 0), G, pe.seq(l, 0), h.device)
+        x_sorted, local_off, recv_counts = kernels.ep_receive(pe.recv_rows(l), E, G, cap)
+        y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden, self.inter)
+        kernels.ep_return_p2p(y_sorted, recv_counts, E, G, self.rank, cap, pe.peer_table(l, 1),
+                              pe.peer_table(l, 3), pe.seq(l, 1), pe.done(l, 1))
+        kernels.ep_wait_p2p(pe.own_flags(l, 1), G, pe.seq(l, 1), h.device)
+        return kernels.combine(pe.back_rows(l), slot_ep, idx, w)
+

@@ -383,3 +383,42 @@ def ep_return(y_sorted: torch.Tensor, recv_counts: torch.Tensor, num_experts: in
     check(_native.lib().moe_ep_return(_p(y_sorted), _p(recv_counts), num_experts, world, cap, H,
                                       _p(y_back), _stream(dev)), "moe_ep_return")
     return y_back
+
+
+# ---------------------------------------------------------------------------
+# Expert-parallel exchange over peer memory (see moeinfra_b200.ep_p2p)
+# ---------------------------------------------------------------------------
+
+def ep_dispatch_p2p(h: torch.Tensor, offsets: torch.Tensor, pair_token: torch.Tensor,
+                    pair_slot: torch.Tensor, k: int, num_experts: int, world: int, rank: int,
+                    cap: int, peer_recv: int, peer_flags: int, seq: int, done: int) -> torch.Tensor:
+    """Rows straight into the owners' receive regions, then signal; returns pair_slot_ep."""
+    dev = _need_cuda("ep_dispatch_p2p", h=h, offsets=offsets)
+    T, H = h.shape
+    slot_ep = torch.empty(T * k, dtype=torch.int32, device=dev)
+    check(_native.lib().moe_ep_dispatch_p2p(_p(h), _p(offsets), _p(pair_token), _p(pair_slot), T,
+                                            k, num_experts, world, rank, cap, H,
+                                            ctypes.c_void_p(peer_recv), ctypes.c_void_p(peer_flags),
+                                            ctypes.c_void_p(seq), ctypes.c_void_p(done),
+                                            _p(slot_ep), _stream(dev)), "moe_ep_dispatch_p2p")
+    return slot_ep
+
+
+def ep_return_p2p(y_sorted: torch.Tensor, recv_counts: torch.Tensor, num_experts: int, world: int,
+                  rank: int, cap: int, peer_back: int, peer_flags: int, seq: int, done: int) -> None:
+    dev = _need_cuda("ep_return_p2p", y_sorted=y_sorted, recv_counts=recv_counts)
+    check(_native.lib().moe_ep_return_p2p(_p(y_sorted), _p(recv_counts), num_experts, world, rank,
+                                          cap, y_sorted.shape[1], ctypes.c_void_p(peer_back),
+                                          ctypes.c_void_p(peer_flags), ctypes.c_void_p(seq),
+                                          ctypes.c_void_p(done), _stream(dev)), "moe_ep_return_p2p")
+
+
+def ep_wait_p2p(flags: int, world: int, seq: int, device: torch.device) -> None:
+    check(_native.lib().moe_ep_wait_p2p(ctypes.c_void_p(flags), world, ctypes.c_void_p(seq),
+                                        _stream(device)), "moe_ep_wait_p2p")
+
+
+def ep_receive_rows(recv_rows: torch.Tensor, num_experts: int, world: int, cap: int):
+    """:func:`ep_receive` on a receive region that is a view (peer-memory exchange)."""
+    return ep_receive(recv_rows, num_experts, world, cap)
+

@@ -47,6 +47,10 @@ class MoELayer:
         # Routing of the last offloaded call (device int64 [T, k]); None after a
         # resident call.  The engine hands it to the prefetcher.
         self.last_expert_indices: Optional[torch.Tensor] = None
+        # Read the device error word at the offload path's sync point (one more
+        # stream synchronisation per call).  An owner that checks at its own
+        # sync points (the engine, once per generation) turns this off.
+        self.check_each_call = True
 
     # -- residency (reference :39-115) -------------------------------------------
     def _ensure_expert_on_gpu(self, expert_id: int):
@@ -176,9 +180,10 @@ class MoELayer:
             else:
                 out = self._per_expert(hidden_states, expert_indices, expert_weights, unique_ids,
                                        gpu_experts)
-            # The offload path synchronises anyway (routing read-back, copies):
-            # surface any error a kernel flagged on the device here.
-            kernels.check_device(hidden_states.device)
+            # The offload path synchronises anyway (routing read-back): surface
+            # any error a kernel flagged on the device here.
+            if self.check_each_call:
+                kernels.check_device(hidden_states.device)
             return out
         finally:
             if self.cache_manager is not None:
