@@ -518,6 +518,8 @@ def run_device(args, rank: int, world: int, local_rank: int):
     else:
         line["ep_parity"] = ep_par
         line["ep_breakdown"] = ep_split
+    if not args.no_extra and not args.no_config4:
+        line["config4"] = measure_config4(dev, rank, world)
     # Kernels flag timed-out waits or codebook mismatches on the device: a run
     # whose launches were invalid must not print a number.
     from moeinfra_b200 import kernels as _k
@@ -673,8 +675,8 @@ class SyntheticMixtral:
     tensors live in one pinned slab each (``pin_expert``).
     """
 
-    def __init__(self, layers: int, device, vocab: int = 32000) -> None:
-        self.layers, self.device, self.vocab = layers, device, vocab
+    def __init__(self, layers: int, device, vocab: int = 32000, pin: bool = True) -> None:
+        self.layers, self.device, self.vocab, self.pin = layers, device, vocab, pin
 
     def load(self) -> None:
         pass
@@ -712,7 +714,8 @@ class SyntheticMixtral:
                         BLOB_KEY: pack_blob({"quant_type": "nf4", "blocksize": 64,
                                              "dtype": "bfloat16", "shape": [rows, cols]})}
         ex = PrequantizedNF4Expert.from_serialized(st["w1"], st["w2"], st["w3"], HIDDEN, FFN)
-        pin_expert(ex)
+        if self.pin:
+            pin_expert(ex)
         return ex
 
 
@@ -782,6 +785,49 @@ def measure_config3(dev):
             "setup_s": round(setup_s, 1),
             "note": "InferenceEngine.generate, 32-layer random-init Mixtral-8x7B, 40 random ids -> "
                     "32 greedy tokens, 4 GiB GPU expert cache (LRU), pinned CPU tier, eager decode"}
+
+
+def measure_config4(dev, rank: int, world: int):
+    """Config 4: the 32-layer Mixtral-8x7B, experts resident and sharded over the GPUs.
+
+    64 sequences x 512 random-id prompt tokens, then 128 greedy tokens; rank r
+    serves sequences [r*64/G, (r+1)*64/G) and owns experts [r*8/G, (r+1)*8/G)
+    of every layer (one expert per GPU per layer at G = 8).  Prefill exchanges
+    tokens with NCCL all-to-alls, decode steps through peer memory inside a
+    CUDA graph of the whole step.  One GPU: the same model with every expert
+    resident and the fused single-GPU layers.  Times are max over ranks.
+    """
+    from moeinfra_b200.engine.engine import InferenceEngine
+    from moeinfra_b200.engine.types import ForwardRequest
+    B, S, N = 64, 512, 128
+    Bl = B // world
+    cfg = {"model": {"name": None, "num_layers": LAYERS, "num_experts": EXPERTS,
+                     "num_experts_per_tok": TOP_K, "hidden_size": HIDDEN, "intermediate_size": FFN,
+                     "num_attention_heads": 32, "num_key_value_heads": 8, "vocab_size": 32000,
+                     "rope_theta": 1e6, "rms_norm_eps": 1e-5, "device": str(dev)},
+           "cache": {"gpu_slots": LAYERS * EXPERTS, "cpu_slots": LAYERS * EXPERTS},
+           "transfer": {"bandwidth_gbps": 50.0, "staging_slots": 2},
+           "engine": {"max_batch": Bl, "max_seq_len": S + N, "preload_experts": world == 1},
+           "parallel": {"expert_parallel": world > 1}}
+    loader = SyntheticMixtral(LAYERS, dev, pin=False)
+    eng = InferenceEngine(cfg, model_loader=loader)
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, 32000, (B, S), generator=g)[rank * Bl:(rank + 1) * Bl]
+    eng._initialize_runtime()
+    torch.cuda.synchronize()
+    _barrier(world)
+    res = eng.generate(ForwardRequest(input_ids=ids, max_new_tokens=N))
+    prefill = _max_over_ranks(res.ttft_ms, world, dev)
+    decode = _max_over_ranks(res.stage_timings["decode"], world, dev)
+    graphed = res.stage_timings["cuda_graph_decode"]
+    eng.close()
+    del eng
+    torch.cuda.empty_cache()
+    return {"value": round(B * (N - 1) / (decode / 1e3), 1), "unit": "tok/s (decode, bs64 global)",
+            "prefill_ms": round(prefill, 1), "prefill_tok_s": round(B * S / (prefill / 1e3), 1),
+            "decode_ms": round(decode, 1), "cuda_graph_decode": bool(graphed),
+            "sequences_per_gpu": Bl, "note": "InferenceEngine.generate, 32-layer random-init "
+            "Mixtral-8x7B, 64 x 512 random ids -> 128 greedy tokens; max over ranks"}
 
 
 def measure_config0(tables, dev, K: int):
@@ -957,6 +1003,8 @@ def main():
                     help="skip the bs64, prefill, config-0 and config-3 measurements")
     ap.add_argument("--ep-exchange", choices=("p2p", "nccl"), default="p2p",
                     help="expert-parallel token exchange: stores into peer memory, or NCCL")
+    ap.add_argument("--no-config4", action="store_true",
+                    help="skip the config-4 (full model, expert-parallel, bs64) measurement")
     ap.add_argument("--no-offload", action="store_true",
                     help="skip the config-3 (full model, CPU-offloaded experts) measurement")
     args = ap.parse_args()

@@ -24,7 +24,12 @@ Extra config keys (all optional): ``model.{num_attention_heads,
 num_key_value_heads, vocab_size, rope_theta, rms_norm_eps}`` when the
 checkpoint has no ``config.json``; ``cache.gpu_budget_bytes``;
 ``transfer.{prefetch_policy, staging_slots}``; ``engine.{max_batch,
-max_seq_len, cuda_graphs, preload_experts}``.
+max_seq_len, cuda_graphs, preload_experts}``; ``parallel.expert_parallel``:
+one process per GPU (``torch.distributed`` initialised), rank r keeps experts
+``[r*E/G, (r+1)*E/G)`` of every layer resident and runs its own sequences;
+each MoE layer is an ``ExpertParallelMoE`` (peer-memory exchange for decode
+steps, NCCL all-to-all for prefill); every rank must call ``generate`` with
+the same batch shape.
 """
 from __future__ import annotations
 
@@ -111,6 +116,10 @@ class InferenceEngine:
         self._max_len = int(engine_cfg.get("max_seq_len", 2048))
         self._use_graphs = bool(engine_cfg.get("cuda_graphs", True))
         self._preload = bool(engine_cfg.get("preload_experts", False))
+        self._ep = bool(config.get("parallel", {}).get("expert_parallel", False))
+        self._peer = None
+        if self._ep and not (torch.distributed.is_available() and torch.distributed.is_initialized()):
+            raise RuntimeError("parallel.expert_parallel needs an initialised process group")
 
         self._cache_manager = CacheManager(
             gpu_slots=cache_cfg.get("gpu_slots", 8), cpu_slots=cache_cfg.get("cpu_slots", 32),
@@ -150,11 +159,33 @@ class InferenceEngine:
         self._model.load()
         dev = self._device
         layers = []
+        if self._ep:
+            from moeinfra_b200.ep import ExpertParallelMoE, capacity, local_experts
+            from moeinfra_b200.ep_p2p import PeerExchange
+            from moeinfra_b200.transfer.nf4_reconstruct import resident_expert
+            rank = torch.distributed.get_rank()
+            world = torch.distributed.get_world_size()
+            owned = local_experts(rank, self._num_experts, world)
+            if world > 1:
+                self._peer = PeerExchange(self._num_layers, world, rank,
+                                          capacity(self._max_batch, self._num_experts_per_tok,
+                                                   self._num_experts, world), self._hidden,
+                                          device=dev)
         for layer_id in range(self._num_layers):
             w = self._model.load_layer(layer_id)
             router = ExpertRouter(w.moe_gate.to(device=dev, dtype=self._dtype),
                                   num_experts_per_tok=self._num_experts_per_tok,
                                   logger=self._logger)
+            if self._ep:
+                with torch.cuda.device(dev):
+                    local = [resident_expert(self._model.load_expert(layer_id, e), dev)
+                             for e in owned]
+                self._moe_layers.append(ExpertParallelMoE(
+                    router, local, rank=rank, world_size=world,
+                    max_tokens=self._max_batch * self._max_len, peer=self._peer,
+                    layer_slot=layer_id))
+                layers.append(w)
+                continue
             moe = MoELayer(layer_id, router, self._cache_manager, self._model,
                            self._transfer_scheduler, logger=self._logger,
                            prefetch_engine=self._prefetch_engine)
@@ -173,12 +204,14 @@ class InferenceEngine:
         self._runtime_initialized = True
 
     def _after_layer(self, layer_id: int, moe: MoELayer) -> None:
-        idx = moe.last_expert_indices
+        idx = getattr(moe, "last_expert_indices", None)
         if idx is not None:
             self._prefetch_engine.on_layer_complete(layer_id, idx)
 
     def preload_experts(self) -> None:
         """Make every expert GPU-resident now (needs gpu_slots >= layers x experts)."""
+        if self._ep:
+            return  # expert-parallel layers hold their shards resident from the start
         with torch.cuda.device(self._device):
             for moe in self._moe_layers:
                 for e in range(self._num_experts):
@@ -186,6 +219,8 @@ class InferenceEngine:
         torch.cuda.synchronize(self._device)
 
     def all_experts_resident(self) -> bool:
+        if self._ep:
+            return True  # every rank holds its shard of every layer resident
         cm = self._cache_manager
         return all(cm.is_gpu_resident(l, e) for l in range(self._num_layers)
                    for e in range(self._num_experts))
@@ -320,6 +355,11 @@ class InferenceEngine:
         for g, *_ in self._graphs.values():
             g.reset()
         self._graphs.clear()
+        if self._peer is not None:
+            torch.cuda.synchronize(self._device)
+            torch.distributed.barrier()
+            self._peer.close()
+            self._peer = None
 
     def __enter__(self):
         return self

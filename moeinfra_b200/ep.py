@@ -57,8 +57,10 @@ class ExpertParallelMoE:
     def __init__(self, router, experts: Sequence, rank: int, world_size: int, max_tokens: int,
                  group=None, peer=None, layer_slot: int = 0) -> None:
         """``peer`` (a :class:`~moeinfra_b200.ep_p2p.PeerExchange`, optional) switches both
-        exchanges from NCCL all-to-alls to stores into peer memory; ``layer_slot`` picks this
-        layer's regions in it.  Calls with more than ``max_tokens`` tokens are refused."""
+        exchanges from NCCL all-to-alls to stores into peer memory for calls that fit its
+        regions (decode); larger calls (prefill) use NCCL.  ``layer_slot`` picks this layer's
+        regions.  Every rank passes the same token count per call; calls with more than
+        ``max_tokens`` tokens are refused."""
         self.router = router
         self.num_experts = router.num_experts
         self.top_k = router.num_experts_per_tok
@@ -74,8 +76,8 @@ class ExpertParallelMoE:
         self.inter = experts[0].intermediate_size
         self._table = kernels.expert_array([ex.nf4_descriptor for ex in self.experts])
         self.peer, self.layer_slot = peer, layer_slot
-        if peer is not None and (peer.cap < self.cap or peer.world != world_size):
-            raise ValueError("peer exchange regions are smaller than this layer's exchange")
+        if peer is not None and peer.world != world_size:
+            raise ValueError("peer exchange regions belong to another world size")
 
     def __call__(self, h: torch.Tensor) -> torch.Tensor:
         return self.forward(h)
@@ -86,8 +88,13 @@ class ExpertParallelMoE:
         else:  # timing aid: the kernels alone, each rank exchanging with itself
             out.copy_(inp)
 
+    def _cap(self, tokens: int) -> int:
+        """Rows per rank pair for a call of ``tokens`` tokens (every rank passes the same count)."""
+        return capacity(tokens, self.top_k, self.num_experts, self.world)
+
     def _dispatch(self, h: torch.Tensor, exchange: bool = True):
-        E, G, cap, k = self.num_experts, self.world, self.cap, self.top_k
+        E, G, k = self.num_experts, self.world, self.top_k
+        cap = self._cap(h.shape[0])
         _, w, idx = kernels.router_topk(h, self.router.gate_f16(), k, with_logits=False)
         offsets, pair_token, _, pair_slot = kernels.permute(idx, w, E)
         send, slot_ep = kernels.ep_dispatch(h, offsets, pair_token, pair_slot, k, E, G, cap)
@@ -104,8 +111,9 @@ class ExpertParallelMoE:
 
     def exchange_buffers(self, tokens: int):
         """Buffers shaped like one call's two exchanges (for timing the all-to-alls alone)."""
-        rows_d = self.world * (self.cap + 1)
-        rows_r = self.world * self.cap
+        cap = self._cap(tokens)
+        rows_d = self.world * (cap + 1)
+        rows_r = self.world * cap
         dev = self.router.gate_f16().device
         return [torch.empty(r, self.hidden, dtype=torch.float16, device=dev)
                 for r in (rows_d, rows_d, rows_r, rows_r)]
@@ -124,9 +132,9 @@ class ExpertParallelMoE:
         if h.shape[0] > self.max_tokens:
             raise ValueError(f"{h.shape[0]} tokens exceed max_tokens={self.max_tokens}")
         h = h.contiguous()
-        if self.peer is not None and exchange:
+        if self.peer is not None and exchange and self._cap(h.shape[0]) <= self.peer.cap:
             return self._forward_p2p(h)
-        E, G, cap = self.num_experts, self.world, self.cap
+        E, G, cap = self.num_experts, self.world, self._cap(h.shape[0])
         x_sorted, local_off, recv_counts, slot_ep, idx, w = self._dispatch(h, exchange)
         y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden, self.inter)
         y_back = kernels.ep_return(y_sorted, recv_counts, E, G, cap)

@@ -37,10 +37,13 @@ def _align(v: int) -> int:
 
 
 def _check(ret, what: str):
+    """cuda-python returns (status, *values): raise on a bad status, return the values."""
     err = ret[0] if isinstance(ret, tuple) else ret
     if int(err) != 0:
         raise RuntimeError(f"{what} failed: {err}")
-    return ret[1] if isinstance(ret, tuple) and len(ret) == 2 else ret
+    if not isinstance(ret, tuple) or len(ret) == 1:
+        return None
+    return ret[1] if len(ret) == 2 else ret[1:]
 
 
 class PeerExchange:

@@ -138,3 +138,19 @@ class ReconstructedNF4Expert(nn.Module):
     @property
     def size_bytes(self) -> int:
         return sum(l.weight.numel() * l.weight.element_size() for l in (self.w1, self.w2, self.w3))
+
+
+def resident_expert(cpu_expert, device) -> ReconstructedNF4Expert:
+    """A GPU-resident copy of a CPU expert (its canonical NF4 state copied to ``device``)."""
+    from moeinfra_b200.model.nf4_format import canonical_state
+
+    state = {}
+    for name in ("w1", "w2", "w3"):
+        proj = getattr(cpu_expert, name)
+        raw = proj if isinstance(proj, dict) else proj.state
+        c = canonical_state(raw, name)
+        state[name] = {k: (None if v is None else
+                           v if k == "offset" else v.to(device, non_blocking=True))
+                       for k, v in c.items()}
+    return ReconstructedNF4Expert(cpu_expert, state)
+
