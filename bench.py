@@ -633,8 +633,9 @@ def ep_e2e(ep_layers, tokens, dev, L: int, K: int, W: int, world: int):
     ms = _max_over_ranks(a.elapsed_time(b), world, dev)
     return {"value": round(B * K * world / (ms / 1e3), 3), "unit": "tok/s",
             "h2d_bytes_per_step": B * HIDDEN * 2, "d2h_bytes_per_step": B * HIDDEN * 2,
-            "api": "ExpertParallelMoE.forward per layer (eager, NCCL all-to-all), pinned host "
-                   "in/out per rank; max over ranks"}
+            "api": "ExpertParallelMoE.forward per layer (eager; token exchange "
+                   f"{'through peer memory' if ep_layers[0].peer is not None else 'by NCCL all-to-all'}"
+                   "), pinned host in/out per rank; max over ranks"}
 
 
 def ep_parity(ep_layer0, tok, dev, rank: int):

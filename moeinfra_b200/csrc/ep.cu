@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_dispatch(
     int E, int El, int G, int cap, int vpr, uint4* __restrict__ send,
     int32_t* __restrict__ send_counts, int32_t* __restrict__ pair_slot_ep) {
   __shared__ int s_off[kEpMaxExperts + 1];
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x <= E) s_off[threadIdx.x] = offsets[threadIdx.x];
   __syncthreads();
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -122,6 +124,8 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_move(
     const uint4* __restrict__ in, int32_t* __restrict__ counts, int El, int G, int cap,
     int vpr, uint4* __restrict__ out, int32_t* __restrict__ local_offsets) {
   __shared__ RecvPlan pl;
+  pdl_trigger();
+  pdl_wait();
   if (kReceive)
     build_plan(reinterpret_cast<const int32_t*>(in + (int64_t)cap * vpr),
                (int64_t)(cap + 1) * vpr * 4, El, G, cap, pl);
@@ -184,6 +188,8 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_dispatch_p2p(
     const uint64_t* __restrict__ peer_flags, int32_t* seq, int32_t* done,
     int32_t* __restrict__ pair_slot_ep) {
   __shared__ int s_off[kEpMaxExperts + 1];
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x <= E) s_off[threadIdx.x] = offsets[threadIdx.x];
   __syncthreads();
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -222,6 +228,8 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_return_p2p(
     int rank, int cap, int vpr, const uint64_t* __restrict__ peer_back,
     const uint64_t* __restrict__ peer_flags, int32_t* seq, int32_t* done) {
   __shared__ RecvPlan pl;
+  pdl_trigger();
+  pdl_wait();
   build_plan(counts, El, El, G, cap, pl);
   const int64_t total = (int64_t)G * cap * vpr;
   for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total;
@@ -239,6 +247,8 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_return_p2p(
 
 // Bounded wait until every source's flag reaches this rank's sequence number.
 __global__ void k_ep_wait(const int32_t* flags, int G, const int32_t* seq, uint64_t limit_ns) {
+  pdl_trigger();
+  pdl_wait();
   const int s = threadIdx.x;
   if (s >= G) return;
   const int target = *reinterpret_cast<const volatile int32_t*>(seq);
@@ -278,10 +288,11 @@ extern "C" int moe_ep_dispatch(const uint16_t* h, const int32_t* expert_offsets,
   if (T > 0 && (!h || !pair_token || !pair_slot || !pair_slot_ep)) return MOE_ERR_INVALID_ARG;
   if ((T > 0 && !aligned16(h)) || !aligned16(send_rows)) return MOE_ERR_ALIGNMENT;
   const int vpr = hidden / 8;
-  k_ep_dispatch<<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
-                  static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint4*>(h), expert_offsets, pair_token, pair_slot, T * k, E, El, G,
-      cap, vpr, reinterpret_cast<uint4*>(send_rows), send_counts, pair_slot_ep);
+  if (launch_pdl(k_ep_dispatch, grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                 static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(h),
+                 expert_offsets, pair_token, pair_slot, T * k, E, El, G, cap, vpr,
+                 reinterpret_cast<uint4*>(send_rows), send_counts, pair_slot_ep) != cudaSuccess)
+    return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
@@ -294,10 +305,11 @@ extern "C" int moe_ep_receive(const uint16_t* recv_rows, int32_t* recv_counts, i
   if (!recv_rows || !recv_counts || !x_sorted || !local_offsets) return MOE_ERR_INVALID_ARG;
   if (!aligned16(recv_rows) || !aligned16(x_sorted)) return MOE_ERR_ALIGNMENT;
   const int vpr = hidden / 8;
-  k_ep_move<true><<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
-                    static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint4*>(recv_rows), recv_counts, E / G, G, cap, vpr,
-      reinterpret_cast<uint4*>(x_sorted), local_offsets);
+  if (launch_pdl(k_ep_move<true>, grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                 static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(recv_rows),
+                 recv_counts, E / G, G, cap, vpr, reinterpret_cast<uint4*>(x_sorted),
+                 local_offsets) != cudaSuccess)
+    return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
@@ -309,10 +321,11 @@ extern "C" int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_count
   if (!y_sorted || !recv_counts || !y_back) return MOE_ERR_INVALID_ARG;
   if (!aligned16(y_sorted) || !aligned16(y_back)) return MOE_ERR_ALIGNMENT;
   const int vpr = hidden / 8;
-  k_ep_move<false><<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
-                     static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint4*>(y_sorted), const_cast<int32_t*>(recv_counts), E / G, G, cap, vpr,
-      reinterpret_cast<uint4*>(y_back), nullptr);
+  if (launch_pdl(k_ep_move<false>, grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                 static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(y_sorted),
+                 const_cast<int32_t*>(recv_counts), E / G, G, cap, vpr,
+                 reinterpret_cast<uint4*>(y_back), static_cast<int32_t*>(nullptr)) != cudaSuccess)
+    return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
@@ -332,10 +345,11 @@ extern "C" int moe_ep_dispatch_p2p(const uint16_t* h, const int32_t* expert_offs
   if (T > 0 && (!h || !pair_token || !pair_slot || !pair_slot_ep)) return MOE_ERR_INVALID_ARG;
   if (T > 0 && !aligned16(h)) return MOE_ERR_ALIGNMENT;
   const int vpr = hidden / 8;
-  k_ep_dispatch_p2p<<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
-                      static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint4*>(h), expert_offsets, pair_token, pair_slot, T * k, E, El, G,
-      rank, cap, vpr, peer_recv, peer_flags, seq, done, pair_slot_ep);
+  if (launch_pdl(k_ep_dispatch_p2p, grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                 static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(h),
+                 expert_offsets, pair_token, pair_slot, T * k, E, El, G, rank, cap, vpr,
+                 peer_recv, peer_flags, seq, done, pair_slot_ep) != cudaSuccess)
+    return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
@@ -350,10 +364,11 @@ extern "C" int moe_ep_return_p2p(const uint16_t* y_sorted, const int32_t* recv_c
     return MOE_ERR_INVALID_ARG;
   if (!aligned16(y_sorted)) return MOE_ERR_ALIGNMENT;
   const int vpr = hidden / 8;
-  k_ep_return_p2p<<<grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
-                    static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint4*>(y_sorted), recv_counts, E / G, G, rank, cap, vpr, peer_back,
-      peer_flags, seq, done);
+  if (launch_pdl(k_ep_return_p2p, grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                 static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(y_sorted),
+                 recv_counts, E / G, G, rank, cap, vpr, peer_back, peer_flags, seq,
+                 done) != cudaSuccess)
+    return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
@@ -361,7 +376,9 @@ extern "C" int moe_ep_return_p2p(const uint16_t* y_sorted, const int32_t* recv_c
 extern "C" int moe_ep_wait_p2p(const int32_t* flags, int G, const int32_t* seq, void* stream) {
   using namespace moe;
   if (!flags || !seq || G < 1 || G > kEpMaxExperts) return MOE_ERR_INVALID_ARG;
-  k_ep_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, G, seq, wait_limit_ns());
+  if (launch_pdl(k_ep_wait, 1, 32, 0, static_cast<cudaStream_t>(stream), flags, G, seq,
+                 wait_limit_ns()) != cudaSuccess)
+    return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }

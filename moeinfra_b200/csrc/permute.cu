@@ -222,8 +222,10 @@ extern "C" int moe_combine(const uint16_t* y_sorted, const int32_t* pair_slot,
   if (T < 0 || k < 1 || k > 8 || width <= 0) return MOE_ERR_INVALID_ARG;
   if (T == 0) return MOE_OK;
   if (!y_sorted || !pair_slot || !indices || !weights || !out) return MOE_ERR_INVALID_ARG;
-  k_combine<YHalf><<<grid_for(T * width, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      YHalf{y_sorted}, pair_slot, indices, weights, T, k, width, out);
+  if (launch_pdl(k_combine<YHalf>, grid_for(T * width, 256), 256, 0,
+                 static_cast<cudaStream_t>(stream), YHalf{y_sorted}, pair_slot, indices, weights,
+                 T, k, width, out) != cudaSuccess)
+    return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
