@@ -230,6 +230,11 @@ class InferenceEngine:
         """Prefill the prompt, then greedy-decode ``max_new_tokens`` tokens."""
         self._initialize_runtime()
         timings: dict = {}
+        B = request.input_ids.shape[0] if request.input_ids.ndim == 2 else 0
+        if (self._use_graphs and request.max_new_tokens > 1 and 0 < B <= self._max_batch
+                and self.all_experts_resident()):
+            with torch.cuda.device(self._device):
+                self._graph_for(B)  # built once per batch size, outside the timed stages
         torch.cuda.synchronize(self._device)
         t0 = time.perf_counter()
         logits = self._prefill(request.input_ids, request.attention_mask)
