@@ -742,50 +742,70 @@ def measure_config3(dev):
 
     ``InferenceEngine.generate`` with a 4 GiB GPU expert cache (43 Mixtral
     experts, LRU), every expert in the CPU tier in pinned memory; each miss is
-    one H2D copy on the copy stream.  One warm-up generation, then one timed.
+    one H2D copy on the copy stream.  One warm-up generation, then one timed;
+    then the same with next-layer prefetch (the layer's routed experts
+    requested for the next layer on the copy stream while it computes).
     """
     from moeinfra_b200.engine.engine import InferenceEngine
     from moeinfra_b200.engine.types import ForwardRequest
     from moeinfra_b200.transfer.scheduler import EXECUTE_NEXT_PROFILE
     budget = 4 << 30
     slots = budget // EXPERT_BYTES
-    cfg = {"model": {"name": None, "num_layers": LAYERS, "num_experts": EXPERTS,
-                     "num_experts_per_tok": TOP_K, "hidden_size": HIDDEN, "intermediate_size": FFN,
-                     "num_attention_heads": 32, "num_key_value_heads": 8, "vocab_size": 32000,
-                     "rope_theta": 1e6, "rms_norm_eps": 1e-5, "device": str(dev)},
-           "cache": {"gpu_slots": int(slots), "cpu_slots": LAYERS * EXPERTS,
-                     "eviction_policy": "lru", "gpu_budget_bytes": budget},
-           "transfer": {"bandwidth_gbps": 50.0, "max_concurrent_transfers": 2},
-           "engine": {"max_batch": 1, "max_seq_len": 128}}
     loader = SyntheticMixtral(LAYERS, dev)
     t0 = time.perf_counter()
-    eng = InferenceEngine(cfg, model_loader=loader)
-    for l in range(LAYERS):
-        for e in range(EXPERTS):
-            eng.cache_manager.put(l, e, loader.load_expert(l, e), device="cpu")
+    cpu_experts = {(l, e): loader.load_expert(l, e) for l in range(LAYERS) for e in range(EXPERTS)}
     setup_s = time.perf_counter() - t0
-    g = torch.Generator().manual_seed(3)
-    prompt = torch.randint(0, 32000, (1, 40), generator=g)
-    eng.generate(ForwardRequest(input_ids=prompt, max_new_tokens=32))  # warm-up
-    n0 = len(EXECUTE_NEXT_PROFILE)
-    res = eng.generate(ForwardRequest(input_ids=torch.randint(0, 32000, (1, 40), generator=g),
-                                      max_new_tokens=32))
-    prof = EXECUTE_NEXT_PROFILE[n0:]
-    h2d = sum(p.get("bytes_transferred", 0) for p in prof)
-    total_s = (res.ttft_ms + res.stage_timings["decode"]) / 1e3
     peak = pinned_h2d_peak_gbs(dev)
+
+    def run(policy: str):
+        cfg = {"model": {"name": None, "num_layers": LAYERS, "num_experts": EXPERTS,
+                         "num_experts_per_tok": TOP_K, "hidden_size": HIDDEN,
+                         "intermediate_size": FFN, "num_attention_heads": 32,
+                         "num_key_value_heads": 8, "vocab_size": 32000, "rope_theta": 1e6,
+                         "rms_norm_eps": 1e-5, "device": str(dev)},
+               "cache": {"gpu_slots": int(slots), "cpu_slots": LAYERS * EXPERTS,
+                         "eviction_policy": "lru", "gpu_budget_bytes": budget},
+               "transfer": {"bandwidth_gbps": 50.0, "max_concurrent_transfers": 4,
+                            "prefetch_policy": policy, "prefetch_depth": 1},
+               "engine": {"max_batch": 1, "max_seq_len": 128}}
+        eng = InferenceEngine(cfg, model_loader=loader)
+        for (l, e), ex in cpu_experts.items():
+            eng.cache_manager.put(l, e, ex, device="cpu")
+        g = torch.Generator().manual_seed(3)
+        eng.generate(ForwardRequest(input_ids=torch.randint(0, 32000, (1, 40), generator=g),
+                                    max_new_tokens=32))  # warm-up
+        n0 = len(EXECUTE_NEXT_PROFILE)
+        pf0 = eng.prefetch_engine.submitted
+        res = eng.generate(ForwardRequest(input_ids=torch.randint(0, 32000, (1, 40), generator=g),
+                                          max_new_tokens=32))
+        prof = EXECUTE_NEXT_PROFILE[n0:]
+        moved = sum(p.get("bytes_transferred", 0) for p in prof)
+        prefetched = eng.prefetch_engine.submitted - pf0
+        h2d = moved + prefetched * EXPERT_BYTES  # prefetch copies go through submit_async
+        total_s = (res.ttft_ms + res.stage_timings["decode"]) / 1e3
+        eng.close()
+        return res, h2d, total_s, len(prof), prefetched
+
+    res, h2d, total_s, n_sync, _ = run("none")
     gbs = h2d / total_s / 1e9
-    eng.close()
-    del eng
+    out = {"value": round(res.tps, 3), "unit": "tok/s (decode, bs1)",
+           "ttft_ms": round(res.ttft_ms, 1), "decode_ms": round(res.stage_timings["decode"], 1),
+           "experts_moved": n_sync, "h2d_bytes": int(h2d),
+           "h2d_gbs": round(gbs, 2), "pinned_h2d_peak_gbs": round(peak, 2),
+           "host_link_frac": round(gbs / peak, 4), "gpu_expert_slots": int(slots),
+           "setup_s": round(setup_s, 1),
+           "note": "InferenceEngine.generate, 32-layer random-init Mixtral-8x7B, 40 random ids -> "
+                   "32 greedy tokens, 4 GiB GPU expert cache (LRU), pinned CPU tier, eager decode"}
+    res_p, h2d_p, total_p, n_sync_p, n_pf = run("next_layer")
+    out["prefetch_next_layer"] = {
+        "value": round(res_p.tps, 3), "ttft_ms": round(res_p.ttft_ms, 1),
+        "sync_copies": n_sync_p, "prefetch_copies": n_pf,
+        "h2d_gbs": round(h2d_p / total_p / 1e9, 2),
+        "note": "same run with PrefetchEngine NEXT_LAYER: the current layer's routed experts "
+                "requested for the next layer on the copy stream (random routing predicts few)"}
+    del cpu_experts
     torch.cuda.empty_cache()
-    return {"value": round(res.tps, 3), "unit": "tok/s (decode, bs1)",
-            "ttft_ms": round(res.ttft_ms, 1), "decode_ms": round(res.stage_timings["decode"], 1),
-            "experts_moved": len(prof), "h2d_bytes": int(h2d),
-            "h2d_gbs": round(gbs, 2), "pinned_h2d_peak_gbs": round(peak, 2),
-            "host_link_frac": round(gbs / peak, 4), "gpu_expert_slots": int(slots),
-            "setup_s": round(setup_s, 1),
-            "note": "InferenceEngine.generate, 32-layer random-init Mixtral-8x7B, 40 random ids -> "
-                    "32 greedy tokens, 4 GiB GPU expert cache (LRU), pinned CPU tier, eager decode"}
+    return out
 
 
 def measure_config4(dev, rank: int, world: int):
