@@ -173,6 +173,11 @@ int moe_router_topk_from_logits(const uint16_t* logits, int64_t T, int E,
  * dequant-to-bf16-then-fp16-GEMM semantics.
  *   x fp16 [n, hidden]  ->  y fp16 [n, hidden]; weights in tile16 layout.
  * Requires hidden % 64 == 0 (<= 8192) and inter % 64 == 0.
+ * For 9..32 tokens a projection with few 128-row tiles splits its K blocks
+ * over several work units (fp32 partials in the workspace, summed in order by
+ * a second kernel), so one expert keeps every SM streaming; the workspace
+ * size then depends on the current device's SM count: size and call on the
+ * same device.
  */
 size_t moe_expert_workspace_size(int64_t n, int hidden, int inter);
 int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t* x,

@@ -814,8 +814,31 @@ __device__ __forceinline__ Active route_token(const DecodeArgs& a, const uint4 (
     for (int e = 0; e < kRoutePre; ++e)
       if (e < E) dot8_f64(acc[e], hd, first ? wpre[e] : __ldg(wg + (int64_t)e * nvec + v));
   }
+  if (E <= kRoutePre) {
+    // Transposed butterfly: each exchange halves the experts a lane keeps
+    // (lane bit 4 -> experts 4..7 or 0..3, bit 3, bit 2), then two plain
+    // steps; lane l ends with expert (l >> 2) & 7 summed over the warp.
+    static_assert(kRoutePre == 8, "transposed reduction assumes 8 preloaded experts");
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+    double v4[4], v2[2];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const double send = b4 ? acc[q] : acc[q + 4];
+      v4[q] = (b4 ? acc[q + 4] : acc[q]) + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const double send = b3 ? v4[q] : v4[q + 2];
+      v2[q] = (b3 ? v4[q + 2] : v4[q]) + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    double v1 = (b2 ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? v2[0] : v2[1], 4);
+    v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
+    v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+    const int e = (lane >> 2) & 7;
+    if ((lane & 3) == 0 && e < E) part[warp * MOE_MAX_EXPERTS + e] = v1;
+  }
 #pragma unroll 1
-  for (int e = 0; e < E; ++e) {
+  for (int e = E <= kRoutePre ? E : 0; e < E; ++e) {
     double tot = 0.0;
     if (e < kRoutePre) {
 #pragma unroll
@@ -843,8 +866,17 @@ __device__ __forceinline__ Active route_token(const DecodeArgs& a, const uint4 (
     int W = 1;
     while (W < E) W <<= 1;
     double mine = 0.0;
-    if (lane < E)
+    if (E <= 8) {  // lanes e, e+8, e+16, e+24 take four warps each of expert e
+      const int e = lane & 7, w0 = (lane >> 3) * (kWarpsK / 4);
+      if (e < E)
+#pragma unroll
+        for (int w = 0; w < kWarpsK / 4; ++w) mine += rs.part[(w0 + w) * MOE_MAX_EXPERTS + e];
+      mine += __shfl_xor_sync(0xffffffffu, mine, 8);
+      mine += __shfl_xor_sync(0xffffffffu, mine, 16);
+      if (lane >= E) mine = 0.0;
+    } else if (lane < E) {
       for (int w = 0; w < kWarpsK; ++w) mine += rs.part[w * MOE_MAX_EXPERTS + lane];
+    }
     route::finish_token(mine, lane, E, W, k, 0, nullptr, rs.w, rs.idx);
     __syncwarp();
     // Stable counting sort of the k pairs (distinct experts) by expert id.

@@ -36,6 +36,10 @@
 #include "common.cuh"
 
 namespace moe {
+
+// Narrow (split bf16) tiles when the experts average at most 32 tokens.
+bool gemm_narrow(int64_t P, int E) { return P <= (int64_t)32 * E; }
+
 namespace {
 
 constexpr int kBM = 128;           // weight rows per tile (UMMA M)
@@ -105,6 +109,12 @@ struct GemmArgs {
   int rows;                // output rows per expert (I for gate_up, H for down)
   uint16_t* out;           // [P, rows] fp16
   uint64_t wait_ns;        // limit of every bounded wait (moe_set_wait_limit_ns)
+  // Split-K: ksplit > 1 splits every tile's K blocks into ksplit chunks, one
+  // work unit each; a unit writes its fp32 accumulators to
+  // part[((chunk * P + pair) * mats + m) * rows + row] and k_splitk_reduce
+  // applies the epilogue to their in-order sum.
+  int ksplit;
+  float* part;
 };
 
 // ---- PTX wrappers ----------------------------------------------------------
@@ -413,7 +423,9 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
-  const int total = s_base[a.E];
+  const int ks = a.ksplit;
+  const int total = s_base[a.E] * ks;
+  const int kchunk = (nblk + ks - 1) / ks;  // K blocks per split-K unit
 
   if (warp < kDqWarps) {
     // ---------------- dequant producers + epilogue ----------------
@@ -422,7 +434,9 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
     const uint32_t lut_lane = C::kLutWindow ? (kLutWin | (lane * 8)) : lut + (lane & 15) * 8;
     uint32_t g = 0, it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
-      const Tile tl = tile_of<C::kTileN>(t, s_base, s_off, a.E, mtiles);
+      const int kc = t % ks;
+      const Tile tl = tile_of<C::kTileN>(t / ks, s_base, s_off, a.E, mtiles);
+      const int kb_lo = kc * kchunk, kb_hi = min(nblk, kb_lo + kchunk);
       const moe_nf4_expert_t& ex = a.ex.e[tl.e];
       const moe_nf4_matrix_t* mats[2] = {kGate ? &ex.w1 : &ex.w2, &ex.w3};
       const int R = tl.m0 + i;
@@ -441,7 +455,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
       uint32_t qv[kPrefetch][C::kMats][kWords];
       float av[kPrefetch][C::kMats];
       auto load = [&](int kb, uint32_t (*q)[kWords], float* am) {
-        if (kb < nblk) {
+        if (kb < kb_hi) {
 #pragma unroll
           for (int m = 0; m < C::kMats; ++m) {
             const uint8_t* src = qp[m] + (int64_t)kb * 512;
@@ -457,13 +471,13 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
         }
       };
 #pragma unroll
-      for (int d = 0; d < kPrefetch; ++d) load(d, qv[d], av[d]);
+      for (int d = 0; d < kPrefetch; ++d) load(kb_lo + d, qv[d], av[d]);
       bool stop = false;
-      for (int kb0 = 0; kb0 < nblk && !stop; kb0 += kPrefetch) {
+      for (int kb0 = kb_lo; kb0 < kb_hi && !stop; kb0 += kPrefetch) {
 #pragma unroll
         for (int d = 0; d < kPrefetch; ++d) {
           const int kb = kb0 + d;
-          if (kb >= nblk) break;
+          if (kb >= kb_hi) break;
           const int s = g % NS;
           stop = __shfl_sync(0xffffffffu, s_abort, 0) != 0 ||
                  !warp_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1, a.wait_ns);
@@ -560,7 +574,11 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
               g = __uint_as_float(d1[j]);
               if (kGate) u = __uint_as_float(d3[j]);
             }
-            if (kGate) {
+            if (ks > 1) {  // split-K unit: fp32 partials, epilogue after the sum
+              float* pp = a.part + ((int64_t)(kc * s_off[a.E] + p) * C::kMats) * a.rows + row;
+              pp[0] = g;
+              if (kGate) pp[a.rows] = u;
+            } else if (kGate) {
               const uint16_t o = swiglu_f16(f2h(g), f2h(u));
               if constexpr (C::kSplit) {  // h feeds the down projection as hi/lo rows
                 uint16_t hi, lo;
@@ -585,11 +603,13 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
     if (lane == 0) {
       uint32_t g = 0;
       for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x) {
-        const Tile tl = tile_of<C::kTileN>(t, s_base, s_off, a.E, mtiles);
+        const int kc = t % ks;
+        const Tile tl = tile_of<C::kTileN>(t / ks, s_base, s_off, a.E, mtiles);
+        const int kb_lo = kc * kchunk, kb_hi = min(nblk, kb_lo + kchunk);
         const int brows = C::kSplit ? 2 * tl.nt : tl.nt;
         const int nbox = (brows + kBoxRows - 1) / kBoxRows;
         const int row0 = (C::kSplit ? 2 : 1) * (s_off[tl.e] + tl.n0);
-        for (int kb = 0; kb < nblk; ++kb, ++g) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++g) {
           const int s = g % NS;
           if (!s_abort && !mbar_wait(saddr(&s_empty[s]), ((g / NS) & 1) ^ 1, a.wait_ns)) s_abort = 1;
           if (s_abort) break;
@@ -611,7 +631,9 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
       uint32_t g = 0, it = 0;
       bool issued_any = false;
       for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x, ++it) {
-        const Tile tl = tile_of<C::kTileN>(t, s_base, s_off, a.E, mtiles);
+        const int kc = t % ks;
+        const Tile tl = tile_of<C::kTileN>(t / ks, s_base, s_off, a.E, mtiles);
+        const int kb_lo = kc * kchunk, kb_hi = min(nblk, kb_lo + kchunk);
         const int n = ((C::kSplit ? 2 * tl.nt : tl.nt) + 15) & ~15;
         const uint32_t idesc = instr_desc(n, C::kSplit);
         if (!mbar_wait(saddr(&s_accempty), (it & 1) ^ 1, a.wait_ns)) {
@@ -619,7 +641,7 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
           break;
         }
         tc_fence_after();
-        for (int kb = 0; kb < nblk; ++kb, ++g) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++g) {
           const int s = g % NS;
           if (!mbar_wait(saddr(&s_afull[s]), (g / NS) & 1, a.wait_ns) ||
               !mbar_wait(saddr(&s_bfull[s]), (g / NS) & 1, a.wait_ns)) {
@@ -635,10 +657,10 @@ __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
             for (int m = 0; m < C::kMats; ++m) {
               if constexpr (C::kATmem)
                 tc_mma_ta(tmem + m * C::kDCol3, tmem + C::kACol + (s * C::kMats + m) * 32 + kk * 8,
-                          smem_desc(bt + kk * 32), idesc, (kb | kk) != 0);
+                          smem_desc(bt + kk * 32), idesc, kb != kb_lo || kk != 0);
               else
                 tc_mma(tmem + m * C::kDCol3, smem_desc(stage + m * kATile + kk * 32),
-                       smem_desc(bt + kk * 32), idesc, (kb | kk) != 0);
+                       smem_desc(bt + kk * 32), idesc, kb != kb_lo || kk != 0);
             }
           }
           issued_any = true;
@@ -679,6 +701,42 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   }
   return fn;
+}
+
+// Split-K epilogue: the ks fp32 partials of (pair p, row) summed in chunk
+// order, then the tile epilogue -- gate_up: fp16 SwiGLU of the fp16-rounded
+// sums (as bf16 hi/lo rows when `split_rows`, the narrow down projection's
+// input); down: the fp16-rounded sum.
+template <bool kGate>
+__global__ void k_splitk_reduce(const float* __restrict__ part, int ks, int64_t P, int rows,
+                                bool split_rows, uint16_t* __restrict__ out) {
+  constexpr int kMats = kGate ? 2 : 1;
+  const int64_t n = P * rows;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = i / rows;
+    const int row = static_cast<int>(i - p * rows);
+    float g = 0.f, u = 0.f;
+#pragma unroll 8
+    for (int kc = 0; kc < ks; ++kc) {
+      const float* pp = part + (((int64_t)kc * P + p) * kMats) * rows + row;
+      g = kc == 0 ? pp[0] : __fadd_rn(g, pp[0]);
+      if (kGate) u = kc == 0 ? pp[rows] : __fadd_rn(u, pp[rows]);
+    }
+    if (kGate) {
+      const uint16_t o = swiglu_f16(f2h(g), f2h(u));
+      if (split_rows) {
+        uint16_t hi, lo;
+        split_bf16(h2f(o), &hi, &lo);
+        out[(2 * p) * rows + row] = hi;
+        out[(2 * p + 1) * rows + row] = lo;
+      } else {
+        out[p * rows + row] = o;
+      }
+    } else {
+      out[p * rows + row] = f2h(g);
+    }
+  }
 }
 
 // fp16 rows [P, K] -> bf16 rows [2P, K]: row 2p = bf16(x_p), row 2p+1 = the
@@ -729,18 +787,54 @@ int launch_dq(const GemmArgs& a, const CUtensorMap& map, cudaStream_t s) {
 
 // Narrow tiles (on average at most 32 tokens per expert): 16 dequant warps,
 // 32-token tiles of split bf16 rows (an expert with more tokens takes several),
-// deeper pipeline.  Wide tiles: 8 dequant warps, 256-token fp16 tiles.
+// deeper pipeline.  Wide tiles: 8 dequant warps, 256-token fp16 tiles.  With
+// a.ksplit > 1 the units write partials and k_splitk_reduce finishes.
 template <bool kGate>
 int launch_one(const GemmArgs& a, const uint16_t* x, int64_t P, bool narrow, cudaStream_t s) {
   CUtensorMap map;
   if (!make_token_map(&map, x, narrow ? 2 * P : P, a.K, narrow)) return MOE_ERR_CUDA;
-  return narrow ? launch_dq<kGate, 16>(a, map, s) : launch_dq<kGate, 8>(a, map, s);
+  const int st = narrow ? launch_dq<kGate, 16>(a, map, s) : launch_dq<kGate, 8>(a, map, s);
+  if (st != MOE_OK || a.ksplit == 1) return st;
+  const int64_t n = P * a.rows;
+  const int64_t blocks = ceil_div(n, 256);
+  const int grid = static_cast<int>(blocks < sm_count() * 8 ? blocks : sm_count() * 8);
+  k_splitk_reduce<kGate><<<grid, 256, 0, s>>>(a.part, a.ksplit, P, a.rows, narrow && kGate, a.out);
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
+// Split-K factor of one projection of a single-expert call on narrow tiles
+// (rows x K weights, P tokens), 1 otherwise.  A projection with few row
+// tiles leaves SMs idle (one expert's down projection: 32 tiles on 148
+// SMs); ks chunks of K per tile make ks x tiles units.  Picks the ks <= 8
+// (chunks of at least 8 K blocks) with the fewest waves per unit of work,
+// each extra chunk charged 2 % (its partials and pipeline ramp).
+int gemm_ksplit(int64_t P, int E, int rows, int K) {
+  if (E != 1 || !gemm_narrow(P, E)) return 1;
+  const int64_t tiles = (int64_t)(rows / kBM) * ceil_div(P, Cfg<true, true>::kTileN);
+  const int nblk = K / kBK, sms = sm_count();
+  int best = 1;
+  double best_cost = 1e30;
+  for (int ks = 1; ks <= 8 && (ks == 1 || nblk / ks >= 8); ++ks) {
+    const double cost = (double)ceil_div(tiles * ks, sms) / ks + 0.02 * (ks - 1);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = ks;
+    }
+  }
+  return best;
 }
 
 }  // namespace
 
-// Narrow (split bf16) tiles when the experts average at most 32 tokens.
-bool gemm_narrow(int64_t P, int E) { return P <= (int64_t)32 * E; }
+
+// fp32 partial floats a call's split-K units need (0: no split-K).
+size_t gemm_splitk_floats(int64_t P, int E, int hidden, int inter) {
+  const int kg = gemm_ksplit(P, E, inter, hidden), kd = gemm_ksplit(P, E, hidden, inter);
+  const size_t g = kg > 1 ? (size_t)kg * P * 2 * inter : 0;
+  const size_t d = kd > 1 ? (size_t)kd * P * hidden : 0;
+  return g > d ? g : d;
+}
 
 // Shapes the tensor-core path accepts: weight rows (I and H) multiples of 128,
 // K extents multiples of 64, K-major 16-byte-aligned operands.
@@ -750,11 +844,13 @@ bool gemm_supported(int hidden, int inter) {
 }
 
 // h_sorted: [P, inter] fp16 (wide) or [2P, inter] bf16 split rows (narrow);
-// x_split: [2P, hidden] bf16, used (and required) only for narrow tiles.
+// x_split: [2P, hidden] bf16, used (and required) only for narrow tiles;
+// part: gemm_splitk_floats(P, E, hidden, inter) fp32 (null: no split-K).
 int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
                                 const int32_t* expert_offsets, const uint16_t* x_sorted,
                                 int64_t P, int hidden, int inter, uint16_t* h_sorted,
-                                uint16_t* y_sorted, uint16_t* x_split, cudaStream_t s) {
+                                uint16_t* y_sorted, uint16_t* x_split, float* part,
+                                cudaStream_t s) {
   if (E < 1 || E > MOE_MAX_EXPERTS || P < 1) return MOE_ERR_INVALID_ARG;
   if (!gemm_supported(hidden, inter)) return MOE_ERR_UNSUPPORTED;
   if (P > INT32_MAX / 2) return MOE_ERR_UNSUPPORTED;
@@ -773,6 +869,8 @@ int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
   a.rows = inter;
   a.out = h_sorted;
   a.wait_ns = wait_limit_ns();
+  a.part = part;
+  a.ksplit = part ? gemm_ksplit(P, E, inter, hidden) : 1;
   const bool narrow = gemm_narrow(P, E);
   const uint16_t* x_in = x_sorted;
   if (narrow) {
@@ -789,6 +887,7 @@ int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
   a.K = inter;
   a.rows = hidden;
   a.out = y_sorted;
+  a.ksplit = part ? gemm_ksplit(P, E, hidden, inter) : 1;
   return launch_one<false>(a, h_sorted, P, narrow, s);
 }
 

@@ -38,8 +38,10 @@ int launch_combine_partials(const float* part, int S, const int32_t* pair_slot,
 int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
                                 const int32_t* expert_offsets, const uint16_t* x_sorted,
                                 int64_t P, int hidden, int inter, uint16_t* h_sorted,
-                                uint16_t* y_sorted, uint16_t* x_split, cudaStream_t s);
+                                uint16_t* y_sorted, uint16_t* x_split, float* part,
+                                cudaStream_t s);
 bool gemm_narrow(int64_t P, int E);
+size_t gemm_splitk_floats(int64_t P, int E, int hidden, int inter);
 
 namespace {
 
@@ -164,7 +166,7 @@ extern "C" int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
   st = moe_gather_rows(h, b.pair_token, P, hidden, b.x_sorted, s);
   if (st != MOE_OK) return st;
   st = launch_grouped_gemm_experts(experts, E, b.offsets, b.x_sorted, P, hidden, inter, b.h_sorted,
-                                   b.y_sorted, b.x_split, s);
+                                   b.y_sorted, b.x_split, nullptr, s);
   if (st != MOE_OK) return st;
   return moe_combine(b.y_sorted, b.pair_slot, indices, weights, T, k, hidden, out, s);
 }
@@ -177,6 +179,7 @@ struct ExpertBufs {
   float* y_part;
   int32_t* sync;
   uint16_t* x_split;
+  float* part;  // split-K partials of the tensor-core path (null: none)
 };
 size_t carve_expert(unsigned char* ws, int64_t n, int hidden, int inter, ExpertBufs* b) {
   Carver c{ws};
@@ -184,6 +187,8 @@ size_t carve_expert(unsigned char* ws, int64_t n, int hidden, int inter, ExpertB
   const bool narrow = !use_decode_path(n) && gemm_narrow(n, 1);
   b->h = c.take<uint16_t>((size_t)(narrow ? 2 * n : n) * inter);
   b->x_split = narrow ? c.take<uint16_t>((size_t)2 * n * hidden) : nullptr;
+  const size_t part = use_decode_path(n) ? 0 : gemm_splitk_floats(n, 1, hidden, inter);
+  b->part = part ? c.take<float>(part) : nullptr;
   if (use_decode_path(n)) {
     b->y_part = c.take<float>((size_t)n * decode_splits(inter) * hidden);
     b->sync = c.take<int32_t>(decode_sync_words(inter));
@@ -226,7 +231,7 @@ extern "C" int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t
     return launch_reduce_partials(b.y_part, n, decode_splits(inter), hidden, y, s);
   }
   return launch_grouped_gemm_experts(expert, 1, b.offsets, x, n, hidden, inter, b.h, y, b.x_split,
-                                     s);
+                                     b.part, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -284,5 +289,5 @@ extern "C" int moe_experts_forward(const moe_nf4_expert_t* experts, int E,
     return launch_reduce_partials(b.y_part, P, decode_splits(inter), hidden, y_sorted, s);
   }
   return launch_grouped_gemm_experts(experts, E, expert_offsets, x_sorted, P, hidden, inter, b.h,
-                                     y_sorted, b.x_split, s);
+                                     y_sorted, b.x_split, nullptr, s);
 }

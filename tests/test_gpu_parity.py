@@ -234,6 +234,22 @@ def test_expert_forward_gemm_mixtral_shape(n):
     assert _native.take_device_error() == 0
 
 
+# A single expert with few row tiles splits K into chunks (fp32 partials summed
+# in order by a second kernel): equal chunks (H 1024 / I 2048: gate 2 chunks,
+# down 4) and a ragged last chunk (H 1664: 26 K blocks in chunks of 9, 9, 8).
+@pytest.mark.parametrize("H,I,n", [(1024, 2048, 16), (1664, 256, 16), (1024, 2048, 32)])
+def test_expert_forward_gemm_split_k(H, I, n):
+    from moeinfra_b200 import _native
+
+    ex = make_experts(70 + n, 1, H, I, std=0.05)[0]
+    x = np.random.default_rng(H + n).standard_normal((n, H), dtype=np.float32).astype(np.float16)
+    g = gpu_expert(ex, H, I)
+    for _ in range(2):
+        y = g(_t(x)).cpu().numpy()
+        assert_close_fp16(y, onf4.expert_forward(x, ex, H, I), what=f"split-K expert H={H} I={I}")
+    assert _native.take_device_error() == 0
+
+
 # ---------------------------------------------------------------------------
 # Fused layer
 # ---------------------------------------------------------------------------
