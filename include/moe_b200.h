@@ -4,8 +4,9 @@
  * Conventions (every entry point):
  *   - plain pointers and sizes; no torch or C++ types cross this boundary;
  *   - every device pointer is owned by the caller; the library never allocates
- *     device memory (scratch comes from a caller-provided workspace whose size
- *     the *_workspace_size functions report);
+ *     device memory (scratch comes from a caller-provided, 16-byte-aligned
+ *     workspace whose size the *_workspace_size functions report; an unaligned
+ *     one returns MOE_ERR_ALIGNMENT);
  *   - all work is enqueued on the caller's stream (`stream` is a cudaStream_t
  *     passed as void*; NULL means the legacy default stream);
  *   - the return value is a moe_status_t; nothing throws across the ABI;

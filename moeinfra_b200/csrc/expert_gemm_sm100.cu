@@ -706,35 +706,53 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // Split-K epilogue: the ks fp32 partials of (pair p, row) summed in chunk
 // order, then the tile epilogue -- gate_up: fp16 SwiGLU of the fp16-rounded
 // sums (as bf16 hi/lo rows when `split_rows`, the narrow down projection's
-// input); down: the fp16-rounded sum.
+// input); down: the fp16-rounded sum.  A thread takes 4 consecutive rows
+// (rows are multiples of 128): 16-byte partial loads, 8-byte stores.
 template <bool kGate>
 __global__ void k_splitk_reduce(const float* __restrict__ part, int ks, int64_t P, int rows,
                                 bool split_rows, uint16_t* __restrict__ out) {
   constexpr int kMats = kGate ? 2 : 1;
-  const int64_t n = P * rows;
+  const int r4 = rows / 4;
+  const int64_t n = P * r4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t p = i / rows;
-    const int row = static_cast<int>(i - p * rows);
-    float g = 0.f, u = 0.f;
+    const int64_t p = i / r4;
+    const int row = static_cast<int>(i - p * r4) * 4;
+    float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
 #pragma unroll 8
     for (int kc = 0; kc < ks; ++kc) {
       const float* pp = part + (((int64_t)kc * P + p) * kMats) * rows + row;
-      g = kc == 0 ? pp[0] : __fadd_rn(g, pp[0]);
-      if (kGate) u = kc == 0 ? pp[rows] : __fadd_rn(u, pp[rows]);
-    }
-    if (kGate) {
-      const uint16_t o = swiglu_f16(f2h(g), f2h(u));
-      if (split_rows) {
-        uint16_t hi, lo;
-        split_bf16(h2f(o), &hi, &lo);
-        out[(2 * p) * rows + row] = hi;
-        out[(2 * p + 1) * rows + row] = lo;
+      const float4 a = __ldcs(reinterpret_cast<const float4*>(pp));
+      if (kc == 0) {
+        g = a;
       } else {
-        out[p * rows + row] = o;
+        g.x = __fadd_rn(g.x, a.x); g.y = __fadd_rn(g.y, a.y);
+        g.z = __fadd_rn(g.z, a.z); g.w = __fadd_rn(g.w, a.w);
       }
+      if (kGate) {
+        const float4 b = __ldcs(reinterpret_cast<const float4*>(pp + rows));
+        if (kc == 0) {
+          u = b;
+        } else {
+          u.x = __fadd_rn(u.x, b.x); u.y = __fadd_rn(u.y, b.y);
+          u.z = __fadd_rn(u.z, b.z); u.w = __fadd_rn(u.w, b.w);
+        }
+      }
+    }
+    const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+    uint16_t o[4], lo[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      o[c] = kGate ? swiglu_f16(f2h(gv[c]), f2h(uv[c])) : f2h(gv[c]);
+      if (kGate && split_rows) split_bf16(h2f(o[c]), &o[c], &lo[c]);
+    }
+    const uint2 ov = make_uint2(o[0] | (uint32_t)o[1] << 16, o[2] | (uint32_t)o[3] << 16);
+    if (kGate && split_rows) {
+      const uint2 lv = make_uint2(lo[0] | (uint32_t)lo[1] << 16, lo[2] | (uint32_t)lo[3] << 16);
+      *reinterpret_cast<uint2*>(out + (2 * p) * rows + row) = ov;
+      *reinterpret_cast<uint2*>(out + (2 * p + 1) * rows + row) = lv;
     } else {
-      out[p * rows + row] = f2h(g);
+      *reinterpret_cast<uint2*>(out + p * rows + row) = ov;
     }
   }
 }
@@ -795,7 +813,7 @@ int launch_one(const GemmArgs& a, const uint16_t* x, int64_t P, bool narrow, cud
   if (!make_token_map(&map, x, narrow ? 2 * P : P, a.K, narrow)) return MOE_ERR_CUDA;
   const int st = narrow ? launch_dq<kGate, 16>(a, map, s) : launch_dq<kGate, 8>(a, map, s);
   if (st != MOE_OK || a.ksplit == 1) return st;
-  const int64_t n = P * a.rows;
+  const int64_t n = P * (a.rows / 4);
   const int64_t blocks = ceil_div(n, 256);
   const int grid = static_cast<int>(blocks < sm_count() * 8 ? blocks : sm_count() * 8);
   k_splitk_reduce<kGate><<<grid, 256, 0, s>>>(a.part, a.ksplit, P, a.rows, narrow && kGate, a.out);
@@ -803,19 +821,25 @@ int launch_one(const GemmArgs& a, const uint16_t* x, int64_t P, bool narrow, cud
   return MOE_OK;
 }
 
-// Split-K factor of one projection of a single-expert call on narrow tiles
-// (rows x K weights, P tokens), 1 otherwise.  A projection with few row
-// tiles leaves SMs idle (one expert's down projection: 32 tiles on 148
-// SMs); ks chunks of K per tile make ks x tiles units.  Picks the ks <= 8
-// (chunks of at least 8 K blocks) with the fewest waves per unit of work,
-// each extra chunk charged 2 % (its partials and pipeline ramp).
-int gemm_ksplit(int64_t P, int E, int rows, int K) {
-  if (E != 1 || !gemm_narrow(P, E)) return 1;
-  const int64_t tiles = (int64_t)(rows / kBM) * ceil_div(P, Cfg<true, true>::kTileN);
+// Split-K factor of one projection on narrow tiles (rows x K weights, P token
+// rows, E experts), 1 otherwise.  A projection with few row tiles leaves SMs
+// idle (one expert's down projection: 32 tiles on 148 SMs; eight experts'
+// down projection at bs64: 256 tiles, a second wave 40 SMs short); ks chunks
+// of K per tile make ks x tiles units.  With several experts the per-expert
+// token counts are on the device: the count assumes every expert active with
+// one 32-token chunk.  Picks the ks <= 8 (chunks of at least 8 K blocks, fp32
+// partials of at most kSplitKCap bytes) with the fewest waves per unit of
+// work, each extra chunk charged 2 % (its partials and pipeline ramp).
+constexpr size_t kSplitKCap = (size_t)16 << 20;
+int gemm_ksplit(int64_t P, int E, int rows, int K, int mats) {
+  if (!gemm_narrow(P, E)) return 1;
+  const int64_t chunks = E == 1 ? ceil_div(P, Cfg<true, true>::kTileN) : (E < P ? E : P);
+  const int64_t tiles = (int64_t)(rows / kBM) * chunks;
   const int nblk = K / kBK, sms = sm_count();
   int best = 1;
   double best_cost = 1e30;
   for (int ks = 1; ks <= 8 && (ks == 1 || nblk / ks >= 8); ++ks) {
+    if (ks > 1 && (size_t)ks * P * mats * rows * sizeof(float) > kSplitKCap) break;
     const double cost = (double)ceil_div(tiles * ks, sms) / ks + 0.02 * (ks - 1);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
@@ -830,7 +854,7 @@ int gemm_ksplit(int64_t P, int E, int rows, int K) {
 
 // fp32 partial floats a call's split-K units need (0: no split-K).
 size_t gemm_splitk_floats(int64_t P, int E, int hidden, int inter) {
-  const int kg = gemm_ksplit(P, E, inter, hidden), kd = gemm_ksplit(P, E, hidden, inter);
+  const int kg = gemm_ksplit(P, E, inter, hidden, 2), kd = gemm_ksplit(P, E, hidden, inter, 1);
   const size_t g = kg > 1 ? (size_t)kg * P * 2 * inter : 0;
   const size_t d = kd > 1 ? (size_t)kd * P * hidden : 0;
   return g > d ? g : d;
@@ -870,7 +894,7 @@ int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
   a.out = h_sorted;
   a.wait_ns = wait_limit_ns();
   a.part = part;
-  a.ksplit = part ? gemm_ksplit(P, E, inter, hidden) : 1;
+  a.ksplit = part ? gemm_ksplit(P, E, inter, hidden, 2) : 1;
   const bool narrow = gemm_narrow(P, E);
   const uint16_t* x_in = x_sorted;
   if (narrow) {
@@ -887,7 +911,7 @@ int launch_grouped_gemm_experts(const moe_nf4_expert_t* experts, int E,
   a.K = inter;
   a.rows = hidden;
   a.out = y_sorted;
-  a.ksplit = part ? gemm_ksplit(P, E, hidden, inter) : 1;
+  a.ksplit = part ? gemm_ksplit(P, E, hidden, inter, 1) : 1;
   return launch_one<false>(a, h_sorted, P, narrow, s);
 }
 

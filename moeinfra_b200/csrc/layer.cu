@@ -73,6 +73,7 @@ struct LayerBufs {
   uint16_t* x_sorted;  // grouped-GEMM path
   uint16_t* y_sorted;  // grouped-GEMM path
   uint16_t* x_split;   // grouped-GEMM path, narrow tiles: tokens as bf16 hi/lo rows
+  float* part;         // grouped-GEMM path: split-K partials (null: none)
 };
 
 // The narrow grouped GEMM keeps the SwiGLU activations as bf16 hi/lo row pairs
@@ -80,8 +81,10 @@ struct LayerBufs {
 // A call of P pairs can take narrow tiles only if P <= 32 x MOE_MAX_EXPERTS.
 bool may_be_narrow(int64_t P) { return P <= (int64_t)32 * MOE_MAX_EXPERTS; }
 
+// split_k: room for the grouped GEMM's split-K partials (the size the
+// workspace query reports); a call whose workspace is smaller runs without.
 size_t carve_layer(unsigned char* ws, int64_t T, int hidden, int inter, int E, int k,
-                   LayerBufs* b) {
+                   LayerBufs* b, bool split_k = true) {
   Carver c{ws};
   const int64_t P = T * k;
   b->offsets = c.take<int32_t>(E + 1);
@@ -102,6 +105,8 @@ size_t carve_layer(unsigned char* ws, int64_t T, int hidden, int inter, int E, i
     b->y_sorted = c.take<uint16_t>((size_t)P * hidden);
     if (narrow) b->x_split = c.take<uint16_t>((size_t)2 * P * hidden);
   }
+  const size_t part = use_decode_path(T) || !split_k ? 0 : gemm_splitk_floats(P, E, hidden, inter);
+  b->part = part ? c.take<float>(part) : nullptr;
   return c.used;
 }
 
@@ -119,6 +124,15 @@ bool experts_aligned(const moe_nf4_expert_t* ex, int E) {
 }
 
 }  // namespace
+}  // namespace moe
+
+namespace moe {
+// Workspace bytes of a layer call, with or without the split-K partials.
+size_t layer_workspace_bytes(int64_t T, int hidden, int inter, int E, int k, bool split_k) {
+  LayerBufs b;
+  if (T < 0 || E < 1 || k < 1) return 0;
+  return carve_layer(nullptr, T, hidden, inter, E, k, &b, split_k);
+}
 }  // namespace moe
 
 extern "C" size_t moe_layer_workspace_size(int64_t T, int hidden, int inter, int E, int k) {
@@ -139,8 +153,11 @@ extern "C" int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
   if (!h || !wg || !experts || !out || !indices || !weights) return MOE_ERR_INVALID_ARG;
   if (!experts_aligned(experts, E) || !aligned16(h) || !aligned16(out)) return MOE_ERR_ALIGNMENT;
   LayerBufs b;
-  const size_t need = carve_layer(static_cast<unsigned char*>(workspace), T, hidden, inter, E, k, &b);
+  const bool split_k = workspace_bytes >= carve_layer(nullptr, T, hidden, inter, E, k, &b);
+  const size_t need = carve_layer(static_cast<unsigned char*>(workspace), T, hidden, inter, E, k,
+                                  &b, split_k);
   if (!workspace || workspace_bytes < need) return MOE_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return MOE_ERR_ALIGNMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (T == 1 && E <= MOE_MAX_EXPERTS) {
     // One token: counters zeroed, then a single launch (route, experts, combine).
@@ -166,7 +183,7 @@ extern "C" int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
   st = moe_gather_rows(h, b.pair_token, P, hidden, b.x_sorted, s);
   if (st != MOE_OK) return st;
   st = launch_grouped_gemm_experts(experts, E, b.offsets, b.x_sorted, P, hidden, inter, b.h_sorted,
-                                   b.y_sorted, b.x_split, nullptr, s);
+                                   b.y_sorted, b.x_split, b.part, s);
   if (st != MOE_OK) return st;
   return moe_combine(b.y_sorted, b.pair_slot, indices, weights, T, k, hidden, out, s);
 }
@@ -220,6 +237,7 @@ extern "C" int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t
   ExpertBufs b;
   const size_t need = carve_expert(static_cast<unsigned char*>(workspace), n, hidden, inter, &b);
   if (!workspace || workspace_bytes < need) return MOE_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return MOE_ERR_ALIGNMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int st = launch_identity_offsets(b.offsets, static_cast<int>(n), b.sync,
                                    b.sync ? decode_sync_words(inter) : 0, s);
@@ -279,6 +297,7 @@ extern "C" int moe_experts_forward(const moe_nf4_expert_t* experts, int E,
   StageBufs b;
   const size_t need = carve_stage(static_cast<unsigned char*>(workspace), P, hidden, inter, &b);
   if (!workspace || workspace_bytes < need) return MOE_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return MOE_ERR_ALIGNMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (use_decode_path(P)) {
     int st = launch_zero_words(b.sync, decode_sync_words(inter), s);

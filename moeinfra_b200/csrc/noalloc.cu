@@ -52,11 +52,12 @@ extern "C" int moe_layer_forward_noalloc(const uint16_t* h, const uint16_t* wg,
   if (T < 0 || E < 1 || E > MOE_MAX_EXPERTS || k < 1 || k > E || k > 8) return MOE_ERR_INVALID_ARG;
   if (!decode_supported(hidden, inter)) return MOE_ERR_UNSUPPORTED;
   if (T == 0) return MOE_OK;
-  const size_t need = moe_layer_workspace_size(T, hidden, inter, E, k);
-  if (need > kNoAllocScratch) return MOE_ERR_WORKSPACE;
+  // The layer's optional split-K partials are used only when they fit too.
+  if (layer_workspace_bytes(T, hidden, inter, E, k, false) > kNoAllocScratch)
+    return MOE_ERR_WORKSPACE;
   void* scratch = nullptr;
   const int st = scratch_address(&scratch);
   if (st != MOE_OK) return st;
   return moe_layer_forward(h, wg, experts, E, k, T, hidden, inter, out, indices, weights, scratch,
-                           need, stream);
+                           kNoAllocScratch, stream);
 }

@@ -69,6 +69,24 @@ def test_host_validation_rejects_bad_arguments_without_launching():
     assert lib.moe_router_topk(None, None, 0, 4096, 8, 2, None, None, None, None) == 0
 
 
+def test_unaligned_workspace_is_rejected_before_any_launch():
+    """Workspace entry points return MOE_ERR_ALIGNMENT for a workspace that is
+    not 16-byte aligned (the split-K partials are read as 16-byte vectors);
+    the pointers below are never dereferenced: the check precedes every launch."""
+    lib = _native.lib()
+    fake = 0x100000
+    m = _native.NF4Matrix(fake, fake, fake)
+    desc = _native.NF4Expert(m, m, m)
+    need = lib.moe_expert_workspace_size(16, 4096, 14336)
+    st = lib.moe_expert_forward(ctypes.byref(desc), ctypes.c_void_p(fake), 16, 4096, 14336,
+                                ctypes.c_void_p(fake), ctypes.c_void_p(fake + 8), need, None)
+    assert st == 5  # MOE_ERR_ALIGNMENT
+    # too small a workspace is reported first
+    st = lib.moe_expert_forward(ctypes.byref(desc), ctypes.c_void_p(fake), 16, 4096, 14336,
+                                ctypes.c_void_p(fake), ctypes.c_void_p(fake), need - 1, None)
+    assert st == 4  # MOE_ERR_WORKSPACE
+
+
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_native, "_lib", None)
     monkeypatch.setenv("MOE_B200_LIB", str(tmp_path / "nope.so"))
