@@ -205,6 +205,9 @@ int moe_expert_forward(const moe_nf4_expert_t* expert, const uint16_t* x,
  *   receive the routing (both required).
  * The workspace needs no initialisation (the layer zeroes the counters it
  * keeps there); calls sharing a workspace must be ordered on the device.
+ * For 9 or more tokens on narrow tiles (at most 32 per expert) the size
+ * reported includes split-K partials for projections with few row tiles; a
+ * smaller workspace that still holds everything else runs without them.
  * T == 1 runs as two launches: the counters, then one kernel that routes,
  * runs both projections and combines.  That kernel's CTAs (one per SM) wait
  * on one another's progress, so it needs the whole GPU's SMs; every such wait
@@ -228,9 +231,10 @@ int moe_layer_forward(const uint16_t* h, const uint16_t* wg,
  * grows mid-step stalls the step).  Scratch comes from a file-scope device
  * array of MOE_NOALLOC_SCRATCH_BYTES (4 MiB) per device: enough for
  * T*k <= 16 routed pairs at Mixtral shapes (hidden 4096, inter 14336), i.e.
- * decode batches up to 8 tokens with top-2.  A call whose
- * moe_layer_workspace_size() exceeds it returns MOE_ERR_WORKSPACE and does
- * nothing.  The array's address is looked up (cudaGetSymbolAddress) on the
+ * decode batches up to 8 tokens with top-2.  A call whose workspace need
+ * (without the optional split-K partials, which moe_layer_forward uses only
+ * when its workspace holds them) exceeds it returns MOE_ERR_WORKSPACE and
+ * does nothing.  The array's address is looked up (cudaGetSymbolAddress) on the
  * first call on each device and cached; make that first call before any
  * stream capture on the device.  The scratch used is the CURRENT device's
  * (cudaGetDevice), which must be the device `stream` belongs to; the cached

@@ -16,6 +16,8 @@
 
 namespace moe {
 bool decode_supported(int hidden, int inter);  // expert_decode.cu
+size_t layer_workspace_bytes(int64_t T, int hidden, int inter, int E, int k,
+                             bool split_k);  // layer.cu
 
 namespace {
 
