@@ -346,6 +346,9 @@ int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_counts, int E,
  * moe_ep_return_p2p: moe_ep_return that stores the rows for source s straight
  *   into s's return region (G chunks of cap rows) at chunk `rank`, then
  *   signals like the dispatch.
+ * moe_ep_receive_p2p / moe_combine_p2p: moe_ep_receive / moe_combine with
+ *   that wait inside the kernel (every CTA waits, bounded, on the G flags
+ *   before it reads the region): one launch each instead of two.
  * Calls of one exchange must not overlap; give every layer its own regions.
  */
 int moe_ep_dispatch_p2p(const uint16_t* h, const int32_t* expert_offsets,
@@ -357,6 +360,12 @@ int moe_ep_return_p2p(const uint16_t* y_sorted, const int32_t* recv_counts, int 
                       int rank, int cap, int hidden, const uint64_t* peer_back,
                       const uint64_t* peer_flags, int32_t* seq, int32_t* done, void* stream);
 int moe_ep_wait_p2p(const int32_t* flags, int G, const int32_t* seq, void* stream);
+int moe_ep_receive_p2p(const uint16_t* recv_rows, int32_t* recv_counts, int E, int G,
+                       int cap, int hidden, uint16_t* x_sorted, int32_t* local_offsets,
+                       const int32_t* flags, const int32_t* seq, void* stream);
+int moe_combine_p2p(const uint16_t* y_back, const int32_t* pair_slot, const int64_t* indices,
+                    const float* weights, int64_t T, int k, int width, uint16_t* out,
+                    const int32_t* flags, int G, const int32_t* seq, void* stream);
 
 #ifdef __cplusplus
 }

@@ -76,6 +76,10 @@ SIGNATURES: dict[str, tuple] = {
     "moe_ep_return_p2p": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
                                   c_void_p, c_void_p, c_void_p, c_void_p]),
     "moe_ep_wait_p2p": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "moe_ep_receive_p2p": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                   c_void_p, c_void_p, c_void_p, c_void_p]),
+    "moe_combine_p2p": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
+                                c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

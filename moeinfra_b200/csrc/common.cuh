@@ -80,6 +80,23 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// Bounded wait of thread `s` until peer flag s reaches this rank's sequence
+// number *seq (release-stored by the peer at system scope; read with
+// acquire).  false once limit_ns of %globaltimer ran out.
+__device__ __forceinline__ bool wait_peer_flag(const int32_t* flags, int s, const int32_t* seq,
+                                               uint64_t limit_ns) {
+  const int target = *reinterpret_cast<const volatile int32_t*>(seq);
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
+  if (v >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    __nanosleep(200);
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
+    if (v >= target) return true;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
 // Device error word bits (read and cleared by moe_take_device_error).
 constexpr int kErrWaitTimeout = 1;    // a bounded wait ran out
 constexpr int kErrCodebook = 2;       // experts of one launch carry different codebooks

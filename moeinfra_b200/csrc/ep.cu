@@ -22,6 +22,8 @@
 namespace moe {
 namespace {
 
+MOE_DEFINE_ERROR_WORD()
+
 constexpr int kEpMaxExperts = 32;
 constexpr int kEpThreads = 256;
 
@@ -119,13 +121,21 @@ __device__ __forceinline__ int64_t recv_dst(const RecvPlan& pl, int El, int s, i
 // kReceive: `in` is the received buffer (G chunks of cap + 1 rows, counts in
 // each chunk's header row); writes x_sorted, local offsets and the compact
 // counts.  Otherwise: `counts` is that compact copy and `in` is y_sorted.
+// wait_flags (peer-memory exchange): every CTA first waits (bounded) until
+// all G flags reach *wait_seq, i.e. every source's rows have landed.
 template <bool kReceive>
 __global__ void __launch_bounds__(kEpThreads) k_ep_move(
     const uint4* __restrict__ in, int32_t* __restrict__ counts, int El, int G, int cap,
-    int vpr, uint4* __restrict__ out, int32_t* __restrict__ local_offsets) {
+    int vpr, uint4* __restrict__ out, int32_t* __restrict__ local_offsets,
+    const int32_t* wait_flags, const int32_t* wait_seq, uint64_t wait_ns) {
   __shared__ RecvPlan pl;
   pdl_trigger();
   pdl_wait();
+  if (wait_flags) {
+    if (threadIdx.x < G && !wait_peer_flag(wait_flags, threadIdx.x, wait_seq, wait_ns))
+      set_device_error(kErrWaitTimeout);
+    __syncthreads();
+  }
   if (kReceive)
     build_plan(reinterpret_cast<const int32_t*>(in + (int64_t)cap * vpr),
                (int64_t)(cap + 1) * vpr * 4, El, G, cap, pl);
@@ -160,8 +170,6 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_move(
 // receiver waits (bounded) until all G flags reach its own sequence number
 // (each rank sends once and receives once per exchange, so the numbers agree)
 // and then reads its region with the ordinary receive / combine kernels.
-
-MOE_DEFINE_ERROR_WORD()
 
 __device__ __forceinline__ void signal_peers(const uint64_t* __restrict__ peer_flags, int G,
                                              int rank, int32_t* seq, int32_t* done) {
@@ -250,21 +258,7 @@ __global__ void k_ep_wait(const int32_t* flags, int G, const int32_t* seq, uint6
   pdl_trigger();
   pdl_wait();
   const int s = threadIdx.x;
-  if (s >= G) return;
-  const int target = *reinterpret_cast<const volatile int32_t*>(seq);
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
-  if (v >= target) return;
-  const uint64_t t0 = globaltimer_ns();
-  for (;;) {
-    __nanosleep(200);
-    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
-    if (v >= target) return;
-    if (globaltimer_ns() - t0 > limit_ns) {
-      set_device_error(kErrWaitTimeout);
-      return;
-    }
-  }
+  if (s < G && !wait_peer_flag(flags, s, seq, limit_ns)) set_device_error(kErrWaitTimeout);
 }
 
 // The header row must hold E/G int32 counts: hidden * 2 >= 4 * E / G.
@@ -297,10 +291,11 @@ extern "C" int moe_ep_dispatch(const uint16_t* h, const int32_t* expert_offsets,
   return MOE_OK;
 }
 
-extern "C" int moe_ep_receive(const uint16_t* recv_rows, int32_t* recv_counts, int E, int G,
-                              int cap, int hidden, uint16_t* x_sorted, int32_t* local_offsets,
-                              void* stream) {
-  using namespace moe;
+namespace moe {
+namespace {
+int ep_receive(const uint16_t* recv_rows, int32_t* recv_counts, int E, int G, int cap, int hidden,
+               uint16_t* x_sorted, int32_t* local_offsets, const int32_t* flags,
+               const int32_t* seq, void* stream) {
   if (!ep_args_ok(E, G, cap, hidden)) return MOE_ERR_INVALID_ARG;
   if (!recv_rows || !recv_counts || !x_sorted || !local_offsets) return MOE_ERR_INVALID_ARG;
   if (!aligned16(recv_rows) || !aligned16(x_sorted)) return MOE_ERR_ALIGNMENT;
@@ -308,10 +303,28 @@ extern "C" int moe_ep_receive(const uint16_t* recv_rows, int32_t* recv_counts, i
   if (launch_pdl(k_ep_move<true>, grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
                  static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(recv_rows),
                  recv_counts, E / G, G, cap, vpr, reinterpret_cast<uint4*>(x_sorted),
-                 local_offsets) != cudaSuccess)
+                 local_offsets, flags, seq, wait_limit_ns()) != cudaSuccess)
     return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
+}
+}  // namespace
+}  // namespace moe
+
+extern "C" int moe_ep_receive(const uint16_t* recv_rows, int32_t* recv_counts, int E, int G,
+                              int cap, int hidden, uint16_t* x_sorted, int32_t* local_offsets,
+                              void* stream) {
+  return moe::ep_receive(recv_rows, recv_counts, E, G, cap, hidden, x_sorted, local_offsets,
+                         nullptr, nullptr, stream);
+}
+
+extern "C" int moe_ep_receive_p2p(const uint16_t* recv_rows, int32_t* recv_counts, int E, int G,
+                                  int cap, int hidden, uint16_t* x_sorted,
+                                  int32_t* local_offsets, const int32_t* flags,
+                                  const int32_t* seq, void* stream) {
+  if (!flags || !seq) return MOE_ERR_INVALID_ARG;
+  return moe::ep_receive(recv_rows, recv_counts, E, G, cap, hidden, x_sorted, local_offsets,
+                         flags, seq, stream);
 }
 
 extern "C" int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_counts, int E, int G,
@@ -324,7 +337,9 @@ extern "C" int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_count
   if (launch_pdl(k_ep_move<false>, grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
                  static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(y_sorted),
                  const_cast<int32_t*>(recv_counts), E / G, G, cap, vpr,
-                 reinterpret_cast<uint4*>(y_back), static_cast<int32_t*>(nullptr)) != cudaSuccess)
+                 reinterpret_cast<uint4*>(y_back), static_cast<int32_t*>(nullptr),
+                 static_cast<const int32_t*>(nullptr), static_cast<const int32_t*>(nullptr),
+                 uint64_t{0}) != cudaSuccess)
     return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;

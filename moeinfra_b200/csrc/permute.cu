@@ -119,12 +119,23 @@ struct YPartials {
   }
 };
 
+MOE_DEFINE_ERROR_WORD()
+
+// wait_flags (peer-memory exchange): every CTA first waits (bounded) until all
+// wait_G flags reach *wait_seq, i.e. every owner's results have landed.
 template <class Y>
 __global__ void k_combine(Y ysrc, const int32_t* __restrict__ pair_slot,
                           const int64_t* __restrict__ indices, const float* __restrict__ weights,
-                          int64_t T, int k, int width, uint16_t* __restrict__ out) {
+                          int64_t T, int k, int width, uint16_t* __restrict__ out,
+                          const int32_t* wait_flags, int wait_G, const int32_t* wait_seq,
+                          uint64_t wait_ns) {
   pdl_trigger();
   pdl_wait();
+  if (wait_flags) {
+    if (threadIdx.x < wait_G && !wait_peer_flag(wait_flags, threadIdx.x, wait_seq, wait_ns))
+      set_device_error(kErrWaitTimeout);
+    __syncthreads();
+  }
   const int64_t total = T * width;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -167,7 +178,9 @@ int launch_combine_partials(const float* part, int S, const int32_t* pair_slot,
                             const int64_t* indices, const float* weights, int64_t T, int k,
                             int width, uint16_t* out, cudaStream_t s) {
   if (launch_pdl(k_combine<YPartials>, grid_for(T * width, 256), 256, 0, s, YPartials{part, S},
-                 pair_slot, indices, weights, T, k, width, out) != cudaSuccess)
+                 pair_slot, indices, weights, T, k, width, out,
+                 static_cast<const int32_t*>(nullptr), 0, static_cast<const int32_t*>(nullptr),
+                 uint64_t{0}) != cudaSuccess)
     return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
@@ -215,17 +228,36 @@ extern "C" int moe_gather_rows(const uint16_t* rows_in, const int32_t* index, in
                                  static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int moe_combine(const uint16_t* y_sorted, const int32_t* pair_slot,
-                           const int64_t* indices, const float* weights, int64_t T, int k,
-                           int width, uint16_t* out, void* stream) {
-  using namespace moe;
+namespace moe {
+namespace {
+int combine_half(const uint16_t* y_sorted, const int32_t* pair_slot, const int64_t* indices,
+                 const float* weights, int64_t T, int k, int width, uint16_t* out,
+                 const int32_t* flags, int G, const int32_t* seq, void* stream) {
   if (T < 0 || k < 1 || k > 8 || width <= 0) return MOE_ERR_INVALID_ARG;
   if (T == 0) return MOE_OK;
   if (!y_sorted || !pair_slot || !indices || !weights || !out) return MOE_ERR_INVALID_ARG;
   if (launch_pdl(k_combine<YHalf>, grid_for(T * width, 256), 256, 0,
                  static_cast<cudaStream_t>(stream), YHalf{y_sorted}, pair_slot, indices, weights,
-                 T, k, width, out) != cudaSuccess)
+                 T, k, width, out, flags, G, seq, wait_limit_ns()) != cudaSuccess)
     return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;
+}
+}  // namespace
+}  // namespace moe
+
+extern "C" int moe_combine(const uint16_t* y_sorted, const int32_t* pair_slot,
+                           const int64_t* indices, const float* weights, int64_t T, int k,
+                           int width, uint16_t* out, void* stream) {
+  return moe::combine_half(y_sorted, pair_slot, indices, weights, T, k, width, out, nullptr, 0,
+                           nullptr, stream);
+}
+
+extern "C" int moe_combine_p2p(const uint16_t* y_back, const int32_t* pair_slot,
+                               const int64_t* indices, const float* weights, int64_t T, int k,
+                               int width, uint16_t* out, const int32_t* flags, int G,
+                               const int32_t* seq, void* stream) {
+  if (!flags || !seq || G < 1 || G > MOE_MAX_EXPERTS) return MOE_ERR_INVALID_ARG;
+  return moe::combine_half(y_back, pair_slot, indices, weights, T, k, width, out, flags, G, seq,
+                           stream);
 }

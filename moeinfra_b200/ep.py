@@ -151,11 +151,11 @@ class ExpertParallelMoE:
         slot_ep = kernels.ep_dispatch_p2p(h, offsets, pair_token, pair_slot, k, E, G, self.rank,
                                           cap, pe.peer_table(l, 0), pe.peer_table(l, 2),
                                           pe.seq(l, 0), pe.done(l, 0))
-        kernels.ep_wait_p2p(pe.own_flags(l, 0), G, pe.seq(l, 0), h.device)
-        x_sorted, local_off, recv_counts = kernels.ep_receive(pe.recv_rows(l), E, G, cap)
+        x_sorted, local_off, recv_counts = kernels.ep_receive_p2p(pe.recv_rows(l), E, G, cap,
+                                                                  pe.own_flags(l, 0), pe.seq(l, 0))
         y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden, self.inter)
         kernels.ep_return_p2p(y_sorted, recv_counts, E, G, self.rank, cap, pe.peer_table(l, 1),
                               pe.peer_table(l, 3), pe.seq(l, 1), pe.done(l, 1))
-        kernels.ep_wait_p2p(pe.own_flags(l, 1), G, pe.seq(l, 1), h.device)
-        return kernels.combine(pe.back_rows(l), slot_ep, idx, w)
+        return kernels.combine_p2p(pe.back_rows(l), slot_ep, idx, w, G, pe.own_flags(l, 1),
+                                   pe.seq(l, 1))
 

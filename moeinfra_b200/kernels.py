@@ -422,3 +422,35 @@ def ep_receive_rows(recv_rows: torch.Tensor, num_experts: int, world: int, cap: 
     """:func:`ep_receive` on a receive region that is a view (peer-memory exchange)."""
     return ep_receive(recv_rows, num_experts, world, cap)
 
+
+def ep_receive_p2p(recv_rows: torch.Tensor, num_experts: int, world: int, cap: int, flags: int,
+                   seq: int):
+    """:func:`ep_receive` of a peer-memory receive region, waiting (bounded, in the kernel)
+    for all ``world`` flags at ``flags`` to reach ``*seq`` first."""
+    dev = _need_cuda("ep_receive_p2p", recv_rows=recv_rows)
+    H = recv_rows.shape[1]
+    x = torch.empty(world * cap, H, dtype=torch.float16, device=dev)
+    off = torch.empty(num_experts // world + 1, dtype=torch.int32, device=dev)
+    counts = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    check(_native.lib().moe_ep_receive_p2p(_p(recv_rows), _p(counts), num_experts, world, cap, H,
+                                           _p(x), _p(off), ctypes.c_void_p(flags),
+                                           ctypes.c_void_p(seq), _stream(dev)),
+          "moe_ep_receive_p2p")
+    return x, off, counts
+
+
+def combine_p2p(y_back: torch.Tensor, pair_slot: torch.Tensor, indices: torch.Tensor,
+                weights: torch.Tensor, world: int, flags: int, seq: int) -> torch.Tensor:
+    """:func:`combine` of a peer-memory return region, waiting (bounded, in the kernel) for all
+    ``world`` flags at ``flags`` to reach ``*seq`` first."""
+    dev = _need_cuda("combine_p2p", y_back=y_back, pair_slot=pair_slot, indices=indices,
+                     weights=weights)
+    _need_dtype("combine_p2p", y_back, torch.float16, "y_back")
+    T, k = indices.shape
+    width = y_back.shape[1]
+    out = torch.empty(T, width, dtype=torch.float16, device=dev)
+    check(_native.lib().moe_combine_p2p(_p(y_back), _p(pair_slot), _p(indices), _p(weights), T,
+                                        k, width, _p(out), ctypes.c_void_p(flags), world,
+                                        ctypes.c_void_p(seq), _stream(dev)), "moe_combine_p2p")
+    return out
+
