@@ -505,10 +505,12 @@ __device__ __forceinline__ void gate_phase(const DecodeArgs& a, const Active& ac
   };
   // Warp 0 walks the prefetch cursor; its lane 0 pulls the whole 16-row tile
   // (W1, W3, both absmax) of an item kPrefetchGate ahead into L2 when that
-  // item starts a tile.
+  // item starts a tile, up to the CTA's last item (past it the tiles are the
+  // next CTA's, long since streamed).
   Cursor pf = ld;
+  int pf_i = first;
   auto prefetch = [&]() {
-    if (pf.ai < act.n && (pf.r & 1) == 0) {
+    if (pf_i++ < last && pf.ai < act.n && (pf.r & 1) == 0) {
       const moe_nf4_expert_t& ex = a.ex.e[s_active[pf.ai]];
       const uint32_t tile = pf.r >> 1;
       const uint32_t qbytes = 16u * (H / 2), abytes = 16u * (H / 64) * 4u;
@@ -654,10 +656,11 @@ __device__ __forceinline__ void down_phase(const DecodeArgs& a, const Active& ac
     }
   };
   // Warp 0 walks the prefetch cursor; its lane 0 pulls an upcoming item's
-  // blocks (contiguous in tile16) into L2.
+  // blocks (contiguous in tile16) into L2, up to the CTA's last item.
   int p_ai = c_first_ai, p_s = c_first_s, p_rg = c_first_rg;
+  int p_i = first;
   auto prefetch = [&]() {
-    if (p_ai < act.n) {
+    if (p_i++ < last && p_ai < act.n) {
       const moe_nf4_expert_t& ex = a.ex.e[s_active[p_ai]];
       const int b0 = p_s * kSplitBlocks, b1 = min(b0 + kSplitBlocks, nblk);
       const bool p = lane == 0;
