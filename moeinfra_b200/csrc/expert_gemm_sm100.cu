@@ -46,10 +46,11 @@ constexpr int kBM = 128;           // weight rows per tile (UMMA M)
 constexpr int kBK = 64;            // K per stage: one NF4 block
 constexpr int kMaxN = 256;         // tokens per tile (UMMA N, max)
 constexpr int kBoxRows = 64;       // token rows per TMA box
-// Dequant warps per CTA: 8 when the tiles are wide (prefill: shared-memory
-// bandwidth bounds, more warps do not help), 16 when they are narrow (decode
-// batches of ~16 tokens per expert: the dequant arithmetic bounds).  Warp w
-// takes rows 32*(w%4).. and part w/4 of the row's 32 packed bytes.
+// Dequant warps per CTA: 8 for wide and narrow tiles.  Warp w takes rows
+// 32*(w%4).. and part w/4 of the row's 32 packed bytes: a thread loads 16
+// bytes of a row per K step (lanes 32 bytes apart).  Narrow tiles are bound
+// by the L1 load/store data pipe, and 16 warps with 8-byte loads cost it more
+// wavefronts per byte (569 -> 522 us per bs64 layer going from 16 to 8).
 template <int DQ>
 constexpr int threads_for() { return (DQ + 2) * 32; }
 constexpr uint32_t kATile = kBM * kBK * 2;         // 16 KB fp16, swizzled
@@ -335,10 +336,10 @@ __device__ __forceinline__ Tile tile_of(int t, const int* s_base, const int* s_o
   return Tile{e, m * kBM, n0, nt};
 }
 
-template <bool kGate, int kDqWarps>
+template <bool kGate, int kDqWarps, bool kNarrowCfg>
 __global__ void __launch_bounds__(threads_for<kDqWarps>(), 1)
     k_grouped_gemm(const __grid_constant__ GemmArgs a, const __grid_constant__ CUtensorMap tmap) {
-  using C = Cfg<kGate, kDqWarps == 16>;
+  using C = Cfg<kGate, kNarrowCfg>;
   constexpr int kPrefetch = C::kPrefetch;
   constexpr int kThreads = threads_for<kDqWarps>();
   constexpr int kParts = kDqWarps / 4;  // parts of a row's 32 packed bytes
@@ -787,31 +788,31 @@ bool make_token_map(CUtensorMap* map, const uint16_t* x, int64_t rows_total, int
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool kGate, int DQ>
+template <bool kGate, int DQ, bool kN>
 bool gemm_attr() {
-  return cudaFuncSetAttribute(k_grouped_gemm<kGate, DQ>,
+  return cudaFuncSetAttribute(k_grouped_gemm<kGate, DQ, kN>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              Cfg<kGate, DQ == 16>::kSmem) == cudaSuccess;
+                              Cfg<kGate, kN>::kSmem) == cudaSuccess;
 }
 
-template <bool kGate, int DQ>
+template <bool kGate, int DQ, bool kN>
 int launch_dq(const GemmArgs& a, const CUtensorMap& map, cudaStream_t s) {
-  if (!once_per_device(reinterpret_cast<const void*>(&gemm_attr<kGate, DQ>), &gemm_attr<kGate, DQ>))
+  if (!once_per_device(reinterpret_cast<const void*>(&gemm_attr<kGate, DQ, kN>), &gemm_attr<kGate, DQ, kN>))
     return MOE_ERR_CUDA;
-  k_grouped_gemm<kGate, DQ><<<sm_count(), threads_for<DQ>(), Cfg<kGate, DQ == 16>::kSmem, s>>>(a, map);
+  k_grouped_gemm<kGate, DQ, kN><<<sm_count(), threads_for<DQ>(), Cfg<kGate, kN>::kSmem, s>>>(a, map);
   MOE_CHECK_LAUNCH();
   return MOE_OK;
 }
 
-// Narrow tiles (on average at most 32 tokens per expert): 16 dequant warps,
-// 32-token tiles of split bf16 rows (an expert with more tokens takes several),
-// deeper pipeline.  Wide tiles: 8 dequant warps, 256-token fp16 tiles.  With
+// Narrow tiles (on average at most 32 tokens per expert): 32-token tiles of
+// split bf16 rows (an expert with more tokens takes several), deeper pipeline.
+// Wide tiles: 256-token fp16 tiles.  With
 // a.ksplit > 1 the units write partials and k_splitk_reduce finishes.
 template <bool kGate>
 int launch_one(const GemmArgs& a, const uint16_t* x, int64_t P, bool narrow, cudaStream_t s) {
   CUtensorMap map;
   if (!make_token_map(&map, x, narrow ? 2 * P : P, a.K, narrow)) return MOE_ERR_CUDA;
-  const int st = narrow ? launch_dq<kGate, 16>(a, map, s) : launch_dq<kGate, 8>(a, map, s);
+  const int st = narrow ? launch_dq<kGate, 8, true>(a, map, s) : launch_dq<kGate, 8, false>(a, map, s);
   if (st != MOE_OK || a.ksplit == 1) return st;
   const int64_t n = P * (a.rows / 4);
   const int64_t blocks = ceil_div(n, 256);
