@@ -642,16 +642,24 @@ def ep_parity(ep_layer0, tok, dev, rank: int):
     """Layer 0 on every rank: the expert-parallel output vs the single-GPU layer.
 
     Each rank builds all eight experts of layer 0 locally and runs the fused
-    single-GPU layer on its own tokens; the expert-parallel path must agree
-    within the layer tolerance (rel-L2 <= 2e-3, max-abs <= 1e-2 x max(1,|ref|);
-    per-expert token counts differ between the two, which can switch an
-    expert between the 1-row and multi-row semantics).  Worst over ranks.
+    single-GPU layer on the global batch (every rank's step-0 tokens, gathered
+    in rank order), then compares its own rows with the expert-parallel
+    output.  An expert then sees the same tokens in both (the 1-row or
+    multi-row weight semantics follow its token count), so the two agree
+    exactly; the check allows the layer tolerance (rel-L2 <= 2e-3, max-abs
+    <= 1e-2 x max(1,|ref|)).  Worst over ranks.
     """
     from moeinfra_b200 import kernels
+    world = torch.distributed.get_world_size()
     full = [resident_expert(0, e, dev) for e in range(EXPERTS)]
     table = kernels.expert_array([x.nf4_descriptor for x in full])
-    want, idx, _ = kernels.layer_forward(tok, ep_layer0.router.gate_f16(), table, TOP_K, HIDDEN,
-                                         FFN)
+    parts = [torch.empty_like(tok) for _ in range(world)]
+    torch.distributed.all_gather(parts, tok.contiguous())
+    everyone = torch.cat(parts, 0)
+    want_all, _, _ = kernels.layer_forward(everyone, ep_layer0.router.gate_f16(), table, TOP_K,
+                                           HIDDEN, FFN)
+    B = tok.shape[0]
+    want = want_all[rank * B:(rank + 1) * B]
     got = ep_layer0.forward(tok)
     torch.cuda.synchronize()
     d = (got.float() - want.float())
@@ -663,8 +671,9 @@ def ep_parity(ep_layer0, tok, dev, rank: int):
     torch.distributed.all_reduce(v, op=torch.distributed.ReduceOp.MAX)
     del full, table
     return {"max_abs": float(v[1]), "rel_l2": float(v[0]), "ok": bool(v[2] < 0),
-            "check": "layer 0, each rank's step-0 tokens: expert-parallel vs single-GPU fused "
-                     "layer with all 8 experts local; worst over ranks"}
+            "check": "layer 0: expert-parallel rows of each rank vs the single-GPU fused layer "
+                     "(all 8 experts local) on every rank's step-0 tokens together; worst over "
+                     "ranks"}
 
 
 class SyntheticMixtral:
