@@ -42,6 +42,8 @@ typedef enum moe_status {
 
 #define MOE_MAX_EXPERTS 16
 #define MOE_NF4_BLOCKSIZE 64
+/* Rows an expert stage call (P) may have to run on the decode kernels. */
+#define MOE_DECODE_MAX_ROWS 8
 
 /* One resident NF4-quantized linear layer [rows=out, cols=in] in the tile16
  * device layout (see moe_nf4_tile16): rows % 16 == 0, cols % 64 == 0. */
@@ -264,6 +266,20 @@ int moe_experts_forward(const moe_nf4_expert_t* experts, int E,
                         int64_t P, int hidden, int inter, uint16_t* y_sorted,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* moe_experts_forward for a decode batch (P <= MOE_DECODE_MAX_ROWS; more returns
+ * MOE_ERR_UNSUPPORTED) stopped before its last step: y_part fp32
+ * [P, S, hidden] receives the down projection's S = moe_expert_splits(inter)
+ * K-split partials of every row (rows of no expert are left as they were);
+ * fp16(in-order sum over S) of a row is moe_experts_forward's output row.
+ * For a consumer that sums them itself (moe_ep_return_partials_p2p), one
+ * launch fewer.  Same workspace as moe_experts_forward.  moe_expert_splits:
+ * S for `inter` (2048-element K splits), -1 for an unsupported size. */
+int moe_expert_splits(int inter);
+int moe_experts_forward_partials(const moe_nf4_expert_t* experts, int E,
+                                 const int32_t* expert_offsets, const uint16_t* x_sorted,
+                                 int64_t P, int hidden, int inter, float* y_part,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Building blocks of moe_layer_forward, exported for tests and for the
  * expert-parallel path (dispatch/combine around an all-to-all).
@@ -349,6 +365,18 @@ int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_counts, int E,
  * moe_ep_receive_p2p / moe_combine_p2p: moe_ep_receive / moe_combine with
  *   that wait inside the kernel (every CTA waits, bounded, on the G flags
  *   before it reads the region): one launch each instead of two.
+ * moe_ep_front_p2p: the router (moe_router_topk), moe_permute and
+ *   moe_ep_dispatch_p2p in one launch, for 0 <= T <= the GPU's SM count
+ *   (more returns MOE_ERR_UNSUPPORTED): one CTA routes each token with the
+ *   router kernel's arithmetic, the CTAs meet at a grid barrier on `bar`
+ *   (two int32 of this rank, zero before first use; left consistent by every
+ *   call), then each stores its token's row into the owners' regions at the
+ *   sorted position moe_permute gives it.  Outputs weights fp32 / indices
+ *   int64 [T, k] (the router's) and pair_slot_ep [T*k] (moe_ep_dispatch's),
+ *   bit-identical to the three calls it replaces.  k <= 8.
+ * moe_ep_return_partials_p2p: moe_ep_return_p2p that reads the fp32 split
+ *   partials of moe_experts_forward_partials (S splits) and stores
+ *   fp16(in-order sum) -- the rows moe_experts_forward would have produced.
  * Calls of one exchange must not overlap; give every layer its own regions.
  */
 int moe_ep_dispatch_p2p(const uint16_t* h, const int32_t* expert_offsets,
@@ -366,6 +394,14 @@ int moe_ep_receive_p2p(const uint16_t* recv_rows, int32_t* recv_counts, int E, i
 int moe_combine_p2p(const uint16_t* y_back, const int32_t* pair_slot, const int64_t* indices,
                     const float* weights, int64_t T, int k, int width, uint16_t* out,
                     const int32_t* flags, int G, const int32_t* seq, void* stream);
+int moe_ep_front_p2p(const uint16_t* h, const uint16_t* wg, int64_t T, int E, int k, int G,
+                     int rank, int cap, int hidden, const uint64_t* peer_recv,
+                     const uint64_t* peer_flags, int32_t* seq, int32_t* done, int32_t* bar,
+                     float* weights, int64_t* indices, int32_t* pair_slot_ep, void* stream);
+int moe_ep_return_partials_p2p(const float* y_part, int S, const int32_t* recv_counts, int E,
+                               int G, int rank, int cap, int hidden,
+                               const uint64_t* peer_back, const uint64_t* peer_flags,
+                               int32_t* seq, int32_t* done, void* stream);
 
 #ifdef __cplusplus
 }

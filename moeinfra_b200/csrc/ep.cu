@@ -18,6 +18,7 @@
 // and moe_combine applies the reference's ordered fp16 combine
 // (model/moe_layer.py:187-191) unchanged.
 #include "common.cuh"
+#include "router_device.cuh"
 
 namespace moe {
 namespace {
@@ -166,7 +167,8 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_move(
 // spaces.  A sender stores its chunk for rank r straight into r's region at
 // chunk `rank`; when every CTA of the launch has stored (system-scope fence,
 // then a CTA completion count), the last CTA bumps this exchange's local
-// sequence number and release-stores it into flag `rank` of every peer.  The
+// sequence number and, after one system-scope fence, stores it into flag
+// `rank` of every peer (fence then relaxed store: a release pattern).  The
 // receiver waits (bounded) until all G flags reach its own sequence number
 // (each rank sends once and receives once per exchange, so the numbers agree)
 // and then reads its region with the ordinary receive / combine kernels.
@@ -177,12 +179,16 @@ __device__ __forceinline__ void signal_peers(const uint64_t* __restrict__ peer_f
   if (threadIdx.x == 0) {
     __threadfence_system();
     if (atomicAdd(done, 1) == static_cast<int>(gridDim.x) - 1) {
+      // This one system-scope fence orders every CTA's rows (published
+      // through `done`) before all G flag stores, which are therefore plain
+      // relaxed stores issued back to back: a release store per flag would
+      // fence again and wait for the previous flag's NVLink round trip.
       __threadfence_system();
       const int s = *reinterpret_cast<volatile int32_t*>(seq) + 1;
       *reinterpret_cast<volatile int32_t*>(seq) = s;
       for (int r = 0; r < G; ++r) {
         int32_t* f = reinterpret_cast<int32_t*>(peer_flags[r]) + rank;
-        asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f), "r"(s) : "memory");
+        asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(f), "r"(s) : "memory");
       }
       *reinterpret_cast<volatile int32_t*>(done) = 0;
     }
@@ -229,6 +235,121 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_dispatch_p2p(
   signal_peers(peer_flags, G, rank, seq, done);
 }
 
+// Grid-wide meeting point of the n CTAs of one launch (all resident): a
+// sense-reversing barrier on bar[0] (arrivals) and bar[1] (generation), so it
+// needs no reset between launches of any size.  Bounded: false (and the
+// device error bit) when the others did not arrive within limit_ns.
+__device__ bool grid_meet(int32_t* bar, int n, uint64_t limit_ns) {
+  __shared__ int s_ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    volatile int32_t* gen = bar + 1;
+    const int g = *gen;  // read before arriving: it cannot move until this CTA arrives
+    __threadfence();     // orders the read and publishes this CTA's writes
+    bool ok = true;
+    if (atomicAdd(bar, 1) == n - 1) {
+      *reinterpret_cast<volatile int32_t*>(bar) = 0;
+      __threadfence();
+      atomicExch(bar + 1, g + 1);
+    } else {
+      const uint64_t t0 = globaltimer_ns();
+      int v;
+      for (;;) {
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(bar + 1) : "memory");
+        if (v != g) break;
+        if (globaltimer_ns() - t0 > limit_ns) {
+          ok = false;
+          break;
+        }
+        __nanosleep(100);
+      }
+    }
+    __threadfence();
+    if (!ok) set_device_error(kErrWaitTimeout);
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// The front of the expert-parallel layer for a decode batch in one launch:
+// the router, moe_permute and k_ep_dispatch_p2p fused.  CTA t routes token t
+// (route_token_cta: the router kernel's arithmetic, so weights and indices are
+// the router's bit for bit), the CTAs meet, then each places its token's k
+// pairs where the expert-sorted order puts them (pairs of earlier tokens of
+// the same expert come first, as in the stable sort of moe_permute) and stores
+// the token's row into each owner's receive region; CTA 0 writes the count
+// headers and the last CTA to finish signals the peers.  T <= the SM count
+// (every CTA resident); T == 0 launches one CTA that only signals.
+__global__ void __launch_bounds__(route::kCtaWarps * 32) k_ep_front_p2p(
+    const uint4* __restrict__ h, const uint4* __restrict__ wg, int T, int H, int E, int W,
+    int k, int El, int G, int rank, int cap, int vpr, const uint64_t* __restrict__ peer_recv,
+    const uint64_t* __restrict__ peer_flags, int32_t* seq, int32_t* done, int32_t* bar,
+    float* weights, int64_t* indices, int32_t* __restrict__ pair_slot_ep, uint64_t wait_ns) {
+  __shared__ route::FF s_part[route::kCtaWarps];
+  __shared__ int s_total[kEpMaxExperts], s_before[kEpMaxExperts], s_off[kEpMaxExperts + 1];
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.x;
+  if (t < T) route::route_token_cta(h, wg, t, H, E, W, k, nullptr, weights, indices, s_part);
+  if (threadIdx.x < E) {
+    s_total[threadIdx.x] = 0;
+    s_before[threadIdx.x] = 0;
+  }
+  if (!grid_meet(bar, gridDim.x, wait_ns)) return;  // the peers' waits run out too (bounded)
+  // Every token's experts, written by the other CTAs above (read through L2).
+  const int P = T * k;
+  const long long* idx = reinterpret_cast<const long long*>(indices);
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    const long long e = __ldcg(idx + p);
+    if (e >= 0 && e < E) {
+      atomicAdd(&s_total[e], 1);
+      if (p < t * k) atomicAdd(&s_before[e], 1);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      s_off[e] = acc;
+      acc += s_total[e];
+    }
+    s_off[E] = acc;
+  }
+  __syncthreads();
+  const int64_t chunk = (int64_t)(cap + 1) * vpr;  // one source's chunk in a receive region
+  if (t == 0 && threadIdx.x < E) {  // header row of the chunk for rank r: r's expert counts
+    const int r = threadIdx.x / El, j = threadIdx.x - r * El;
+    uint4* dst = reinterpret_cast<uint4*>(peer_recv[r]) + rank * chunk + (int64_t)cap * vpr;
+    reinterpret_cast<int32_t*>(dst)[j] = s_total[threadIdx.x];
+  }
+  if (t < T) {
+    // Pair (t, j) of expert e sits at s_off[e] + s_before[e] in the sorted
+    // order (a token's k experts are distinct); rank r = e / El receives it at
+    // row i of this rank's chunk.
+    if (threadIdx.x < k) {
+      const long long e = __ldcg(idx + (int64_t)t * k + threadIdx.x);
+      int32_t slot = -1;
+      if (e >= 0 && e < E) {
+        const int r = static_cast<int>(e) / El;
+        slot = r * cap + (s_off[e] + s_before[e] - s_off[r * El]);
+      }
+      pair_slot_ep[(int64_t)t * k + threadIdx.x] = slot;
+    }
+    for (int v = threadIdx.x; v < k * vpr; v += blockDim.x) {
+      const int j = v / vpr, c = v - j * vpr;
+      const long long e = __ldcg(idx + (int64_t)t * k + j);
+      if (e < 0 || e >= E) continue;
+      const int r = static_cast<int>(e) / El;
+      const int i = s_off[e] + s_before[e] - s_off[r * El];
+      if (i >= cap) continue;
+      uint4* dst = reinterpret_cast<uint4*>(peer_recv[r]) + rank * chunk + (int64_t)i * vpr;
+      dst[c] = h[(int64_t)t * vpr + c];
+    }
+  }
+  signal_peers(peer_flags, G, rank, seq, done);
+}
+
 // Owner side of the return: y rows of source s go to s's return region, chunk
 // `rank`, at the row the source's combine expects (pair_slot_ep layout).
 __global__ void __launch_bounds__(kEpThreads) k_ep_return_p2p(
@@ -249,6 +370,47 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_return_p2p(
     if (src < 0 || src >= (int64_t)G * cap) continue;
     uint4* dst = reinterpret_cast<uint4*>(peer_back[s]) + ((int64_t)rank * cap + i) * vpr;
     dst[c] = y_sorted[src * vpr + c];
+  }
+  signal_peers(peer_flags, G, rank, seq, done);
+}
+
+// k_ep_return_p2p from the expert stage's fp32 split partials ([row][S][H]):
+// each value is the in-order sum over the S splits rounded once to fp16, the
+// arithmetic of the partials reduce that moe_experts_forward ends with, so the
+// rows stored into the peers are the same bits.
+__global__ void __launch_bounds__(kEpThreads) k_ep_return_partials_p2p(
+    const float* __restrict__ part, int S, const int32_t* __restrict__ counts, int El, int G,
+    int rank, int cap, int vpr, const uint64_t* __restrict__ peer_back,
+    const uint64_t* __restrict__ peer_flags, int32_t* seq, int32_t* done) {
+  __shared__ RecvPlan pl;
+  pdl_trigger();
+  pdl_wait();
+  build_plan(counts, El, El, G, cap, pl);
+  const int64_t total = (int64_t)G * cap * vpr;
+  const int64_t width = (int64_t)vpr * 8;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = v / vpr;
+    const int c = static_cast<int>(v - row * vpr);
+    const int s = static_cast<int>(row / cap), i = static_cast<int>(row - (int64_t)s * cap);
+    const int64_t src = recv_dst(pl, El, s, i);
+    if (src < 0 || src >= (int64_t)G * cap) continue;
+    const float4* p = reinterpret_cast<const float4*>(part + src * S * width + (int64_t)c * 8);
+    float4 a = __ldcs(p), b = __ldcs(p + 1);
+    for (int k = 1; k < S; ++k) {
+      const float4 x = __ldcs(p + k * (width / 4)), y = __ldcs(p + k * (width / 4) + 1);
+      a.x = __fadd_rn(a.x, x.x); a.y = __fadd_rn(a.y, x.y);
+      a.z = __fadd_rn(a.z, x.z); a.w = __fadd_rn(a.w, x.w);
+      b.x = __fadd_rn(b.x, y.x); b.y = __fadd_rn(b.y, y.y);
+      b.z = __fadd_rn(b.z, y.z); b.w = __fadd_rn(b.w, y.w);
+    }
+    uint4 o;
+    o.x = (uint32_t)f2h(a.x) | ((uint32_t)f2h(a.y) << 16);
+    o.y = (uint32_t)f2h(a.z) | ((uint32_t)f2h(a.w) << 16);
+    o.z = (uint32_t)f2h(b.x) | ((uint32_t)f2h(b.y) << 16);
+    o.w = (uint32_t)f2h(b.z) | ((uint32_t)f2h(b.w) << 16);
+    uint4* dst = reinterpret_cast<uint4*>(peer_back[s]) + ((int64_t)rank * cap + i) * vpr;
+    dst[c] = o;
   }
   signal_peers(peer_flags, G, rank, seq, done);
 }
@@ -369,6 +531,34 @@ extern "C" int moe_ep_dispatch_p2p(const uint16_t* h, const int32_t* expert_offs
   return MOE_OK;
 }
 
+extern "C" int moe_ep_front_p2p(const uint16_t* h, const uint16_t* wg, int64_t T, int E, int k,
+                                int G, int rank, int cap, int hidden, const uint64_t* peer_recv,
+                                const uint64_t* peer_flags, int32_t* seq, int32_t* done,
+                                int32_t* bar, float* weights, int64_t* indices,
+                                int32_t* pair_slot_ep, void* stream) {
+  using namespace moe;
+  if (T < 0 || k < 1 || k > 8 || k > E || !ep_args_ok(E, G, cap, hidden) || rank < 0 ||
+      rank >= G)
+    return MOE_ERR_INVALID_ARG;
+  const int El = E / G;
+  if (T * (k < El ? k : El) > cap) return MOE_ERR_INVALID_ARG;
+  if (T > sm_count()) return MOE_ERR_UNSUPPORTED;  // every CTA must be resident
+  if (!peer_recv || !peer_flags || !seq || !done || !bar) return MOE_ERR_INVALID_ARG;
+  if (T > 0 && (!h || !wg || !weights || !indices || !pair_slot_ep)) return MOE_ERR_INVALID_ARG;
+  if (T > 0 && (!aligned16(h) || !aligned16(wg))) return MOE_ERR_ALIGNMENT;
+  int W = 1;
+  while (W < E) W <<= 1;
+  const int grid = T > 0 ? static_cast<int>(T) : 1;
+  if (launch_pdl(k_ep_front_p2p, grid, route::kCtaWarps * 32, 0,
+                 static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(h),
+                 reinterpret_cast<const uint4*>(wg), static_cast<int>(T), hidden, E, W, k, El, G,
+                 rank, cap, hidden / 8, peer_recv, peer_flags, seq, done, bar, weights, indices,
+                 pair_slot_ep, wait_limit_ns()) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
 extern "C" int moe_ep_return_p2p(const uint16_t* y_sorted, const int32_t* recv_counts, int E,
                                  int G, int rank, int cap, int hidden, const uint64_t* peer_back,
                                  const uint64_t* peer_flags, int32_t* seq, int32_t* done,
@@ -383,6 +573,25 @@ extern "C" int moe_ep_return_p2p(const uint16_t* y_sorted, const int32_t* recv_c
                  static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(y_sorted),
                  recv_counts, E / G, G, rank, cap, vpr, peer_back, peer_flags, seq,
                  done) != cudaSuccess)
+    return MOE_ERR_CUDA;
+  MOE_CHECK_LAUNCH();
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_return_partials_p2p(const float* y_part, int S, const int32_t* recv_counts,
+                                          int E, int G, int rank, int cap, int hidden,
+                                          const uint64_t* peer_back, const uint64_t* peer_flags,
+                                          int32_t* seq, int32_t* done, void* stream) {
+  using namespace moe;
+  if (S < 1 || !ep_args_ok(E, G, cap, hidden) || rank < 0 || rank >= G)
+    return MOE_ERR_INVALID_ARG;
+  if (!y_part || !recv_counts || !peer_back || !peer_flags || !seq || !done)
+    return MOE_ERR_INVALID_ARG;
+  if (!aligned16(y_part)) return MOE_ERR_ALIGNMENT;
+  const int vpr = hidden / 8;
+  if (launch_pdl(k_ep_return_partials_p2p, grid_rows((int64_t)G * cap * vpr), kEpThreads, 0,
+                 static_cast<cudaStream_t>(stream), y_part, S, recv_counts, E / G, G, rank, cap,
+                 vpr, peer_back, peer_flags, seq, done) != cudaSuccess)
     return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;

@@ -46,6 +46,7 @@ namespace {
 constexpr int kWarpsK = 16;           // warps per CTA, each a K part
 constexpr int kThreadsK = kWarpsK * 32;
 constexpr int kMaxTok = 8;            // tokens per expert on this path
+static_assert(kMaxTok == MOE_DECODE_MAX_ROWS, "decode row bound of the public header");
 constexpr int kDownSlice = 2048;      // K elements per down split
 constexpr uint32_t kLutWin = 0x10000;
 constexpr int kDynSmem = 0x20000;     // dynamic allocation covering the window

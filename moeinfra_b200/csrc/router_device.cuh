@@ -143,5 +143,65 @@ __device__ __forceinline__ void finish_token(double logit, int lane, int E, int 
   topk_renorm(p, lane, E, W, k, t, weights, indices);
 }
 
+// Few tokens: one CTA of kCtaWarps warps per token.  Warp w takes expert
+// w % E and range w / E of the row's 16-byte vectors (kCtaWarps / E ranges),
+// issues its loads ahead of the arithmetic, and sums exactly in double-float;
+// the ranges meet in shared memory (`s_part`, kCtaWarps entries) in a fixed
+// order.  The fp16 logit is the correctly rounded sum, as in the many-token
+// kernel.  Every thread of the CTA calls it (one barrier inside); warp 0
+// writes token t's outputs.
+constexpr int kCtaWarps = 32;
+constexpr int kCtaUnroll = 4;
+
+__device__ __forceinline__ void route_token_cta(const uint4* __restrict__ h,
+                                                const uint4* __restrict__ wg, int64_t t, int H,
+                                                int E, int W, int k, uint16_t* __restrict__ logits,
+                                                float* __restrict__ weights,
+                                                int64_t* __restrict__ indices, FF* s_part) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvec = H >> 3;
+  const int groups = kCtaWarps / E;  // >= 1 for E <= 32
+  if (warp < groups * E) {
+    const int e = warp % E, r = warp / E;
+    const int v0 = static_cast<int>((int64_t)nvec * r / groups);
+    const int v1 = static_cast<int>((int64_t)nvec * (r + 1) / groups);
+    const uint4* hrow = h + t * nvec;
+    const uint4* wrow = wg + (int64_t)e * nvec;
+    FF acc{0.f, 0.f};
+    for (int vb = v0 + lane; vb < v1; vb += 32 * kCtaUnroll) {
+      uint4 hv[kCtaUnroll], wv[kCtaUnroll];
+#pragma unroll
+      for (int u = 0; u < kCtaUnroll; ++u) {
+        const int v = vb + u * 32;
+        hv[u] = v < v1 ? hrow[v] : make_uint4(0, 0, 0, 0);
+        wv[u] = v < v1 ? __ldg(wrow + v) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kCtaUnroll; ++u) {
+        const __half2* hh = reinterpret_cast<const __half2*>(&hv[u]);
+        const __half2* ww = reinterpret_cast<const __half2*>(&wv[u]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 x = __half22float2(hh[q]), y = __half22float2(ww[q]);
+          ff_add(acc, __fmul_rn(x.x, y.x));
+          ff_add(acc, __fmul_rn(x.y, y.y));
+        }
+      }
+    }
+    const FF tot = warp_sum_ff(acc);
+    if (lane == 0) s_part[warp] = tot;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    double mine = 0.0;
+    if (lane < E) {
+      FF tot = s_part[lane];
+      for (int r = 1; r < groups; ++r) ff_merge(tot, s_part[r * E + lane]);
+      mine = ff_value(tot);
+    }
+    finish_token(mine, lane, E, W, k, t, logits, weights, indices);
+  }
+}
+
 }  // namespace route
 }  // namespace moe

@@ -76,6 +76,9 @@ class ExpertParallelMoE:
         self.inter = experts[0].intermediate_size
         self._table = kernels.expert_array([ex.nf4_descriptor for ex in self.experts])
         self.peer, self.layer_slot = peer, layer_slot
+        # The fused front launch runs one CTA per token, all resident at once.
+        self._sms = torch.cuda.get_device_properties(peer.device).multi_processor_count \
+            if peer is not None else 0
         if peer is not None and peer.world != world_size:
             raise ValueError("peer exchange regions belong to another world size")
 
@@ -143,19 +146,38 @@ class ExpertParallelMoE:
         return kernels.combine(y_home, slot_ep, idx, w)
 
     def _forward_p2p(self, h: torch.Tensor) -> torch.Tensor:
-        """The layer with both exchanges as stores into peer memory (no NCCL call)."""
+        """The layer with both exchanges as stores into peer memory (no NCCL call).
+
+        A batch of at most one token per SM takes the fused front launch (router, permute and
+        dispatch in one kernel); a receive of at most ``DECODE_MAX_ROWS`` rows hands the expert
+        stage's fp32 split partials to the return kernel, which sums them on the way out.  Both
+        give the bits of the separate launches."""
         E, G, k, pe, l = self.num_experts, self.world, self.top_k, self.peer, self.layer_slot
         cap = pe.cap
-        _, w, idx = kernels.router_topk(h, self.router.gate_f16(), k, with_logits=False)
-        offsets, pair_token, _, pair_slot = kernels.permute(idx, w, E)
-        slot_ep = kernels.ep_dispatch_p2p(h, offsets, pair_token, pair_slot, k, E, G, self.rank,
-                                          cap, pe.peer_table(l, 0), pe.peer_table(l, 2),
-                                          pe.seq(l, 0), pe.done(l, 0))
+        if h.shape[0] <= self._sms:
+            w, idx, slot_ep = kernels.ep_front_p2p(h, self.router.gate_f16(), k, E, G, self.rank,
+                                                   cap, pe.peer_table(l, 0), pe.peer_table(l, 2),
+                                                   pe.seq(l, 0), pe.done(l, 0), pe.bar(l))
+        else:
+            _, w, idx = kernels.router_topk(h, self.router.gate_f16(), k, with_logits=False)
+            offsets, pair_token, _, pair_slot = kernels.permute(idx, w, E)
+            slot_ep = kernels.ep_dispatch_p2p(h, offsets, pair_token, pair_slot, k, E, G,
+                                              self.rank, cap, pe.peer_table(l, 0),
+                                              pe.peer_table(l, 2), pe.seq(l, 0), pe.done(l, 0))
         x_sorted, local_off, recv_counts = kernels.ep_receive_p2p(pe.recv_rows(l), E, G, cap,
                                                                   pe.own_flags(l, 0), pe.seq(l, 0))
-        y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden, self.inter)
-        kernels.ep_return_p2p(y_sorted, recv_counts, E, G, self.rank, cap, pe.peer_table(l, 1),
-                              pe.peer_table(l, 3), pe.seq(l, 1), pe.done(l, 1))
+        if x_sorted.shape[0] <= kernels.DECODE_MAX_ROWS:
+            part = kernels.experts_forward_partials(self._table, local_off, x_sorted, self.hidden,
+                                                    self.inter)
+            kernels.ep_return_partials_p2p(part, recv_counts, E, G, self.rank, cap,
+                                           pe.peer_table(l, 1), pe.peer_table(l, 3),
+                                           pe.seq(l, 1), pe.done(l, 1))
+        else:
+            y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden,
+                                               self.inter)
+            kernels.ep_return_p2p(y_sorted, recv_counts, E, G, self.rank, cap,
+                                  pe.peer_table(l, 1), pe.peer_table(l, 3), pe.seq(l, 1),
+                                  pe.done(l, 1))
         return kernels.combine_p2p(pe.back_rows(l), slot_ep, idx, w, G, pe.own_flags(l, 1),
                                    pe.seq(l, 1))
 

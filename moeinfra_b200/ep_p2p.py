@@ -9,15 +9,16 @@ expert-parallel layer:
 * a return region: ``G`` chunks of ``cap`` rows (chunk ``s`` from owner rank
   ``s``), what the combine all-to-all would deliver;
 * two int32 flag arrays ``[G]`` (dispatch, return), written by the peers;
-* this rank's own sequence numbers and CTA completion counters.
+* this rank's own sequence numbers, CTA completion counters and the two words
+  of the fused front launch's grid barrier.
 
 The buffer's CUDA IPC handle is exchanged once over the process group (host
 objects, ``all_gather_object``) and each peer's buffer is mapped with
 ``cudaIpcOpenMemHandle`` (plain peer mappings: no multicast object is
-created).  The kernels (``moe_ep_dispatch_p2p``, ``moe_ep_return_p2p``,
-``moe_ep_wait_p2p``) then store token rows straight into the owners' receive
+created).  The kernels (``moe_ep_front_p2p`` or ``moe_ep_dispatch_p2p``,
+``moe_ep_return_partials_p2p`` or ``moe_ep_return_p2p``) then store token rows straight into the owners' receive
 regions and results straight into the sources' return regions, and signal
-with release stores of per-exchange sequence numbers; every wait is bounded
+with per-exchange sequence numbers (one system-scope fence, then the flag stores); every wait is bounded
 (``moe_set_wait_limit_ns``).
 
 Regions are per layer, so consecutive layers never reuse a region while a
@@ -61,7 +62,7 @@ class PeerExchange:
         self.recv_bytes = _align(G * (cap + 1) * hidden * 2)
         self.back_bytes = _align(G * cap * hidden * 2)
         self.flag_bytes = _align(2 * G * 4)
-        self.local_bytes = _align(4 * 4)  # seq[2], done[2]
+        self.local_bytes = _align(6 * 4)  # seq[2], done[2], bar[2]
         self.layer_bytes = self.recv_bytes + self.back_bytes + self.flag_bytes + self.local_bytes
         total = self.layer_bytes * layers
         # Zeroed: flags, sequence numbers and completion counters start at 0.
@@ -127,6 +128,10 @@ class PeerExchange:
 
     def done(self, l: int, d: int) -> int:
         return self.seq(l, d) + 8
+
+    def bar(self, l: int) -> int:
+        """The grid-barrier words (arrivals, generation) of layer ``l``'s front launch."""
+        return self.seq(l, 0) + 16
 
     def close(self) -> None:
         from cuda.bindings import runtime as rt

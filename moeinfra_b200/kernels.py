@@ -51,6 +51,10 @@ def _need_dtype(what: str, t: torch.Tensor, dtype: torch.dtype, name: str) -> No
         raise ValueError(f"{what}: {name} must be {dtype}, got {t.dtype}")
 
 
+# Rows an expert stage call may have on the decode kernels (MOE_DECODE_MAX_ROWS).
+DECODE_MAX_ROWS = 8
+
+
 def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
 
@@ -454,3 +458,60 @@ def combine_p2p(y_back: torch.Tensor, pair_slot: torch.Tensor, indices: torch.Te
                                         ctypes.c_void_p(seq), _stream(dev)), "moe_combine_p2p")
     return out
 
+
+def ep_front_p2p(h: torch.Tensor, gate_f16: torch.Tensor, k: int, num_experts: int, world: int,
+                 rank: int, cap: int, peer_recv: int, peer_flags: int, seq: int, done: int,
+                 bar: int):
+    """Router, permute and the peer-memory dispatch in one launch (``T`` <= the SM count).
+
+    Returns ``(weights fp32 [T, k], indices int64 [T, k], pair_slot_ep int32 [T*k])``, the
+    values :func:`router_topk`, :func:`permute` and :func:`ep_dispatch_p2p` give."""
+    dev = _need_cuda("ep_front_p2p", h=h, gate_f16=gate_f16)
+    _need_dtype("ep_front_p2p", h, torch.float16, "h")
+    _need_dtype("ep_front_p2p", gate_f16, torch.float16, "gate_f16")
+    T, H = h.shape
+    w = torch.empty(T, k, dtype=torch.float32, device=dev)
+    idx = torch.empty(T, k, dtype=torch.int64, device=dev)
+    slot_ep = torch.empty(T * k, dtype=torch.int32, device=dev)
+    check(_native.lib().moe_ep_front_p2p(_p(h), _p(gate_f16), T, num_experts, k, world, rank, cap,
+                                         H, ctypes.c_void_p(peer_recv),
+                                         ctypes.c_void_p(peer_flags), ctypes.c_void_p(seq),
+                                         ctypes.c_void_p(done), ctypes.c_void_p(bar), _p(w),
+                                         _p(idx), _p(slot_ep), _stream(dev)), "moe_ep_front_p2p")
+    return w, idx, slot_ep
+
+
+def expert_splits(inter: int) -> int:
+    """K splits of the decode down projection (its fp32 partials per row)."""
+    return int(_native.lib().moe_expert_splits(inter))
+
+
+def experts_forward_partials(experts, expert_offsets: torch.Tensor, x_sorted: torch.Tensor,
+                             hidden: int, inter: int) -> torch.Tensor:
+    """:func:`experts_forward` of a decode batch (<= 8 rows) up to the down projection's
+    fp32 split partials ``[P, S, hidden]`` (their in-order fp16 sum is the output row)."""
+    dev = _need_cuda("experts_forward_partials", expert_offsets=expert_offsets, x_sorted=x_sorted)
+    _need_dtype("experts_forward_partials", x_sorted, torch.float16, "x_sorted")
+    _need_dtype("experts_forward_partials", expert_offsets, torch.int32, "expert_offsets")
+    P = x_sorted.shape[0]
+    part = torch.empty(P, expert_splits(inter), hidden, dtype=torch.float32, device=dev)
+    lib = _native.lib()
+    ws_bytes = lib.moe_experts_workspace_size(P, hidden, inter)
+    ws = _workspace(ws_bytes, dev)
+    check(lib.moe_experts_forward_partials(experts, len(experts), _p(expert_offsets),
+                                           _p(x_sorted), P, hidden, inter, _p(part), _p(ws),
+                                           ws_bytes, _stream(dev)),
+          "moe_experts_forward_partials")
+    return part
+
+
+def ep_return_partials_p2p(y_part: torch.Tensor, recv_counts: torch.Tensor, num_experts: int,
+                           world: int, rank: int, cap: int, peer_back: int, peer_flags: int,
+                           seq: int, done: int) -> None:
+    """:func:`ep_return_p2p` from :func:`experts_forward_partials`' fp32 partials."""
+    dev = _need_cuda("ep_return_partials_p2p", y_part=y_part, recv_counts=recv_counts)
+    _need_dtype("ep_return_partials_p2p", y_part, torch.float32, "y_part")
+    check(_native.lib().moe_ep_return_partials_p2p(
+        _p(y_part), y_part.shape[1], _p(recv_counts), num_experts, world, rank, cap,
+        y_part.shape[2], ctypes.c_void_p(peer_back), ctypes.c_void_p(peer_flags),
+        ctypes.c_void_p(seq), ctypes.c_void_p(done), _stream(dev)), "moe_ep_return_partials_p2p")

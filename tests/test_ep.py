@@ -185,6 +185,94 @@ def test_ep_kernels_emulated(G, T):
         assert_close_fp16(out.cpu().numpy(), want[s], what=f"EP G={G} rank {s}")
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("G,T", [(2, 1), (4, 1), (8, 1), (4, 2), (2, 5)])
+def test_ep_fused_p2p_kernels_emulated(G, T):
+    """The fused front launch (router + permute + dispatch into peer regions) and the return
+    from split partials, G ranks emulated on one GPU: the "peer" regions are this GPU's own
+    buffers, and every wait is already satisfied when it runs (each kernel that waits is
+    launched after all the signals it waits for).  Bit-identical to the separate launches."""
+    from moeinfra_b200 import _native, kernels
+    from tests.helpers import gpu_expert
+
+    E, H, I, k = 8, 256, 512, 2
+    experts_np = make_experts(5, E, H, I)
+    experts = [gpu_expert(ex, H, I) for ex in experts_np]
+    wg_np = _gate(E, H)
+    wg = torch.from_numpy(wg_np).cuda()
+    hs = [torch.from_numpy(_tokens(s, T, H)).cuda() for s in range(G)]
+    want, _ = expected_outputs([h.cpu().numpy() for h in hs], wg_np, experts_np, H, I, k)
+    cap = ep.capacity(T, k, E, G)
+    El = E // G
+    dev = torch.device("cuda")
+    recv = [torch.zeros(G * (cap + 1), H, dtype=torch.float16, device=dev) for _ in range(G)]
+    back = [torch.zeros(G * cap, H, dtype=torch.float16, device=dev) for _ in range(G)]
+    flags = [torch.zeros(2 * G, dtype=torch.int32, device=dev) for _ in range(G)]
+    words = [torch.zeros(6, dtype=torch.int32, device=dev) for _ in range(G)]  # seq, done, bar
+
+    def table(addrs):
+        return torch.tensor(addrs, dtype=torch.int64, device=dev)
+
+    t_recv = table([r.data_ptr() for r in recv])
+    t_back = table([b.data_ptr() for b in back])
+    t_fd = table([f.data_ptr() for f in flags])
+    t_fr = table([f.data_ptr() + 4 * G for f in flags])
+    front = []
+    for s in range(G):
+        wd = words[s].data_ptr()
+        w, idx, slot_ep = kernels.ep_front_p2p(hs[s], wg, k, E, G, s, cap, t_recv.data_ptr(),
+                                               t_fd.data_ptr(), wd, wd + 8, wd + 16)
+        # the separate launches it replaces
+        _, w_ref, idx_ref = kernels.router_topk(hs[s], wg, k, with_logits=False)
+        off, ptok, _, pslot = kernels.permute(idx_ref, w_ref, E)
+        send, slot_ref = kernels.ep_dispatch(hs[s], off, ptok, pslot, k, E, G, cap)
+        assert torch.equal(w.view(torch.int32), w_ref.view(torch.int32))
+        assert torch.equal(idx, idx_ref)
+        assert torch.equal(slot_ep, slot_ref)
+        front.append((w, idx, slot_ep, send))
+    torch.cuda.synchronize()
+    C = cap + 1
+    for r in range(G):
+        # every source's chunk (header + its rows) as the dispatch all-to-all would deliver it
+        for s in range(G):
+            sent = front[s][3][r * C:(r + 1) * C]
+            got = recv[r][s * C:(s + 1) * C]
+            counts = sent[cap].view(torch.int32)[:El]
+            assert torch.equal(got[cap].view(torch.int32)[:El], counts)
+            n = int(counts.sum())
+            assert torch.equal(got[:n].view(torch.int16), sent[:n].view(torch.int16))
+        assert flags[r][:G].tolist() == [1] * G
+    for r in range(G):
+        wd = words[r].data_ptr()
+        x, local_off, counts = kernels.ep_receive_p2p(recv[r], E, G, cap, flags[r].data_ptr(), wd)
+        tab = kernels.expert_array([experts[e].nf4_descriptor for e in ep.local_experts(r, E, G)])
+        y = kernels.experts_forward(tab, local_off, x, H, I)
+        if G * cap <= kernels.DECODE_MAX_ROWS:
+            part = kernels.experts_forward_partials(tab, local_off, x, H, I)
+            assert part.shape == (G * cap, kernels.expert_splits(I), H)
+            kernels.ep_return_partials_p2p(part, counts, E, G, r, cap, t_back.data_ptr(),
+                                           t_fr.data_ptr(), wd + 4, wd + 12)
+        else:
+            kernels.ep_return_p2p(y, counts, E, G, r, cap, t_back.data_ptr(), t_fr.data_ptr(),
+                                  wd + 4, wd + 12)
+        y_back = kernels.ep_return(y, counts, E, G, cap)
+        torch.cuda.synchronize()
+        _, dst = oep.receive_plan(counts.cpu(), E, G)
+        for s in range(G):
+            m = len(dst[s])
+            assert torch.equal(back[s][r * cap:r * cap + m].view(torch.int16),
+                               y_back[s * cap:s * cap + m].view(torch.int16)), (r, s)
+    for s in range(G):
+        w, idx, slot_ep, _ = front[s]
+        out = kernels.combine_p2p(back[s], slot_ep, idx, w, G, flags[s].data_ptr() + 4 * G,
+                                  words[s].data_ptr() + 4)
+        torch.cuda.synchronize()
+        assert_close_fp16(out.cpu().numpy(), want[s], what=f"fused EP G={G} rank {s}")
+    assert [int(v) for v in words[0][:4].tolist()] == [1, 1, 0, 0]  # seq bumped, done reset
+    assert int(words[0][4]) == 0 and int(words[0][5]) == 1          # barrier: one generation
+    assert _native.stream_check(torch.cuda.current_stream().cuda_stream) == 0
+
+
 # ---------------------------------------------------------------------------
 # NCCL layer on 2+ GPUs
 # ---------------------------------------------------------------------------
@@ -286,6 +374,24 @@ def _p2p_worker(rank: int, world: int, port: int):
         assert torch.equal(y.view(torch.int16), want.view(torch.int16))
         assert _native.stream_check(torch.cuda.current_stream().cuda_stream) == 0
         dist.barrier()
+        # One token per rank: the receive fits the decode kernels, so the expert stage hands
+        # its split partials to the return kernel; still bit-identical to the NCCL layer.
+        peer1 = PeerExchange(L, world, rank, ep.capacity(1, k, E, world), H)
+        one = [ep.ExpertParallelMoE(router, local, rank=rank, world_size=world, max_tokens=1,
+                                    peer=peer1, layer_slot=l) for l in range(L)]
+        ref1 = ep.ExpertParallelMoE(router, local, rank=rank, world_size=world, max_tokens=1)
+        assert world * peer1.cap <= kernels.DECODE_MAX_ROWS
+        for step in range(3):
+            h = torch.from_numpy(_tokens(50 + 10 * rank + step, 1, H)).cuda()
+            for l in range(L):
+                got = one[l](h)
+                want = ref1(h)
+                torch.cuda.synchronize()
+                assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (rank, step, l)
+                h = got
+        assert _native.stream_check(torch.cuda.current_stream().cuda_stream) == 0
+        dist.barrier()
+        peer1.close()
     finally:
         if g is not None:
             del g
