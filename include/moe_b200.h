@@ -8,7 +8,10 @@
  *     workspace whose size the *_workspace_size functions report; an unaligned
  *     one returns MOE_ERR_ALIGNMENT);
  *   - all work is enqueued on the caller's stream (`stream` is a cudaStream_t
- *     passed as void*; NULL means the legacy default stream);
+ *     passed as void*; NULL means the legacy default stream of the current
+ *     device); call with the device that owns the stream and the pointers
+ *     current (cudaSetDevice): a kernel launched on another device would
+ *     dereference the pointers there;
  *   - the return value is a moe_status_t; nothing throws across the ABI;
  *     moe_status_string() turns it into text.
  *
@@ -272,13 +275,18 @@ int moe_experts_forward(const moe_nf4_expert_t* experts, int E,
  * K-split partials of every row (rows of no expert are left as they were);
  * fp16(in-order sum over S) of a row is moe_experts_forward's output row.
  * For a consumer that sums them itself (moe_ep_return_partials_p2p), one
- * launch fewer.  Same workspace as moe_experts_forward.  moe_expert_splits:
- * S for `inter` (2048-element K splits), -1 for an unsupported size. */
+ * launch fewer.  Same workspace as moe_experts_forward.  counters: null, or
+ * moe_experts_counter_words(inter) int32 that an earlier kernel on the stream
+ * zeroed (moe_ep_front_p2p can), which spares the zeroing launch; the call
+ * leaves them non-zero.  moe_expert_splits: S for `inter` (2048-element K
+ * splits); both return -1 for an unsupported size. */
 int moe_expert_splits(int inter);
+int moe_experts_counter_words(int inter);
 int moe_experts_forward_partials(const moe_nf4_expert_t* experts, int E,
                                  const int32_t* expert_offsets, const uint16_t* x_sorted,
                                  int64_t P, int hidden, int inter, float* y_part,
-                                 void* workspace, size_t workspace_bytes, void* stream);
+                                 int32_t* counters, void* workspace, size_t workspace_bytes,
+                                 void* stream);
 
 /* ---------------------------------------------------------------------------
  * Building blocks of moe_layer_forward, exported for tests and for the
@@ -373,7 +381,10 @@ int moe_ep_return(const uint16_t* y_sorted, const int32_t* recv_counts, int E,
  *   call), then each stores its token's row into the owners' regions at the
  *   sorted position moe_permute gives it.  Outputs weights fp32 / indices
  *   int64 [T, k] (the router's) and pair_slot_ep [T*k] (moe_ep_dispatch's),
- *   bit-identical to the three calls it replaces.  k <= 8.
+ *   bit-identical to the three calls it replaces.  k <= 8.  It also zeroes
+ *   n_zero int32 at zero_words (the counters of the expert stage that
+ *   follows; may be 0 / null).  After a timeout the exchange state (flags,
+ *   counters, barrier) is undefined: recreate the regions.
  * moe_ep_return_partials_p2p: moe_ep_return_p2p that reads the fp32 split
  *   partials of moe_experts_forward_partials (S splits) and stores
  *   fp16(in-order sum) -- the rows moe_experts_forward would have produced.
@@ -397,7 +408,8 @@ int moe_combine_p2p(const uint16_t* y_back, const int32_t* pair_slot, const int6
 int moe_ep_front_p2p(const uint16_t* h, const uint16_t* wg, int64_t T, int E, int k, int G,
                      int rank, int cap, int hidden, const uint64_t* peer_recv,
                      const uint64_t* peer_flags, int32_t* seq, int32_t* done, int32_t* bar,
-                     float* weights, int64_t* indices, int32_t* pair_slot_ep, void* stream);
+                     float* weights, int64_t* indices, int32_t* pair_slot_ep,
+                     int32_t* zero_words, int n_zero, void* stream);
 int moe_ep_return_partials_p2p(const float* y_part, int S, const int32_t* recv_counts, int E,
                                int G, int rank, int cap, int hidden,
                                const uint64_t* peer_back, const uint64_t* peer_flags,

@@ -82,14 +82,15 @@ SIGNATURES: dict[str, tuple] = {
                                 c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "moe_ep_front_p2p": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int,
                                  c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                                 c_void_p, c_void_p, c_void_p, c_void_p]),
+                                 c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
     "moe_ep_return_partials_p2p": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
                                            c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                            c_void_p]),
     "moe_expert_splits": (c_int, [c_int]),
+    "moe_experts_counter_words": (c_int, [c_int]),
     "moe_experts_forward_partials": (c_int, [ctypes.POINTER(NF4Expert), c_int, c_void_p, c_void_p,
-                                             c_int64, c_int, c_int, c_void_p, c_void_p, c_size_t,
-                                             c_void_p]),
+                                             c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                             c_size_t, c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -91,7 +91,7 @@ __device__ __forceinline__ bool wait_peer_flag(const int32_t* flags, int s, cons
   if (v >= target) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
-    __nanosleep(200);
+    __nanosleep(64);  // short: the wait sits on the layer's critical path
     asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
     if (v >= target) return true;
     if (globaltimer_ns() - t0 > limit_ns) return false;

@@ -279,18 +279,24 @@ __device__ bool grid_meet(int32_t* bar, int n, uint64_t limit_ns) {
 // pairs where the expert-sorted order puts them (pairs of earlier tokens of
 // the same expert come first, as in the stable sort of moe_permute) and stores
 // the token's row into each owner's receive region; CTA 0 writes the count
-// headers and the last CTA to finish signals the peers.  T <= the SM count
-// (every CTA resident); T == 0 launches one CTA that only signals.
+// headers (and zeroes `nzero` words for the expert stage that follows) and
+// the last CTA to finish signals the peers.  T <= the SM count (every CTA
+// resident); T == 0 launches one CTA that only signals.
 __global__ void __launch_bounds__(route::kCtaWarps * 32) k_ep_front_p2p(
     const uint4* __restrict__ h, const uint4* __restrict__ wg, int T, int H, int E, int W,
     int k, int El, int G, int rank, int cap, int vpr, const uint64_t* __restrict__ peer_recv,
     const uint64_t* __restrict__ peer_flags, int32_t* seq, int32_t* done, int32_t* bar,
-    float* weights, int64_t* indices, int32_t* __restrict__ pair_slot_ep, uint64_t wait_ns) {
+    float* weights, int64_t* indices, int32_t* __restrict__ pair_slot_ep, int32_t* zero,
+    int nzero, uint64_t wait_ns) {
   __shared__ route::FF s_part[route::kCtaWarps];
   __shared__ int s_total[kEpMaxExperts], s_before[kEpMaxExperts], s_off[kEpMaxExperts + 1];
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.x;
+  // The expert stage's completion counters (zeroed here, after the wait: their
+  // previous user finished before the predecessor did).
+  if (t == 0)
+    for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
   if (t < T) route::route_token_cta(h, wg, t, H, E, W, k, nullptr, weights, indices, s_part);
   if (threadIdx.x < E) {
     s_total[threadIdx.x] = 0;
@@ -535,7 +541,8 @@ extern "C" int moe_ep_front_p2p(const uint16_t* h, const uint16_t* wg, int64_t T
                                 int G, int rank, int cap, int hidden, const uint64_t* peer_recv,
                                 const uint64_t* peer_flags, int32_t* seq, int32_t* done,
                                 int32_t* bar, float* weights, int64_t* indices,
-                                int32_t* pair_slot_ep, void* stream) {
+                                int32_t* pair_slot_ep, int32_t* zero_words, int n_zero,
+                                void* stream) {
   using namespace moe;
   if (T < 0 || k < 1 || k > 8 || k > E || !ep_args_ok(E, G, cap, hidden) || rank < 0 ||
       rank >= G)
@@ -544,6 +551,7 @@ extern "C" int moe_ep_front_p2p(const uint16_t* h, const uint16_t* wg, int64_t T
   if (T * (k < El ? k : El) > cap) return MOE_ERR_INVALID_ARG;
   if (T > sm_count()) return MOE_ERR_UNSUPPORTED;  // every CTA must be resident
   if (!peer_recv || !peer_flags || !seq || !done || !bar) return MOE_ERR_INVALID_ARG;
+  if (n_zero < 0 || (n_zero > 0 && !zero_words)) return MOE_ERR_INVALID_ARG;
   if (T > 0 && (!h || !wg || !weights || !indices || !pair_slot_ep)) return MOE_ERR_INVALID_ARG;
   if (T > 0 && (!aligned16(h) || !aligned16(wg))) return MOE_ERR_ALIGNMENT;
   int W = 1;
@@ -553,7 +561,7 @@ extern "C" int moe_ep_front_p2p(const uint16_t* h, const uint16_t* wg, int64_t T
                  static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(h),
                  reinterpret_cast<const uint4*>(wg), static_cast<int>(T), hidden, E, W, k, El, G,
                  rank, cap, hidden / 8, peer_recv, peer_flags, seq, done, bar, weights, indices,
-                 pair_slot_ep, wait_limit_ns()) != cudaSuccess)
+                 pair_slot_ep, zero_words, n_zero, wait_limit_ns()) != cudaSuccess)
     return MOE_ERR_CUDA;
   MOE_CHECK_LAUNCH();
   return MOE_OK;

@@ -315,11 +315,16 @@ extern "C" int moe_expert_splits(int inter) {
   return inter > 0 && inter % 64 == 0 ? moe::decode_splits(inter) : -1;
 }
 
+extern "C" int moe_experts_counter_words(int inter) {
+  return inter > 0 && inter % 64 == 0 ? moe::decode_sync_words(inter) : -1;
+}
+
 extern "C" int moe_experts_forward_partials(const moe_nf4_expert_t* experts, int E,
                                             const int32_t* expert_offsets,
                                             const uint16_t* x_sorted, int64_t P, int hidden,
-                                            int inter, float* y_part, void* workspace,
-                                            size_t workspace_bytes, void* stream) {
+                                            int inter, float* y_part, int32_t* counters,
+                                            void* workspace, size_t workspace_bytes,
+                                            void* stream) {
   using namespace moe;
   if (P < 0 || E < 1 || E > MOE_MAX_EXPERTS) return MOE_ERR_INVALID_ARG;
   if (!shapes_ok(hidden, inter) || !use_decode_path(P)) return MOE_ERR_UNSUPPORTED;
@@ -332,8 +337,12 @@ extern "C" int moe_experts_forward_partials(const moe_nf4_expert_t* experts, int
   if (!workspace || workspace_bytes < need) return MOE_ERR_WORKSPACE;
   if (!aligned16(workspace)) return MOE_ERR_ALIGNMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int st = launch_zero_words(b.sync, decode_sync_words(inter), s);
-  if (st != MOE_OK) return st;
+  // Caller-zeroed counters (e.g. by moe_ep_front_p2p) spare the zeroing launch.
+  int32_t* sync = counters ? counters : b.sync;
+  if (!counters) {
+    const int st = launch_zero_words(b.sync, decode_sync_words(inter), s);
+    if (st != MOE_OK) return st;
+  }
   return launch_decode_experts(experts, E, expert_offsets, nullptr, x_sorted, hidden, inter, b.h,
-                               y_part, b.sync, static_cast<int>(P), s);
+                               y_part, sync, static_cast<int>(P), s);
 }

@@ -79,6 +79,7 @@ class ExpertParallelMoE:
         # The fused front launch runs one CTA per token, all resident at once.
         self._sms = torch.cuda.get_device_properties(peer.device).multi_processor_count \
             if peer is not None else 0
+        self._counters = None  # expert-stage counters the fused front zeroes (decode calls)
         if peer is not None and peer.world != world_size:
             raise ValueError("peer exchange regions belong to another world size")
 
@@ -154,10 +155,18 @@ class ExpertParallelMoE:
         give the bits of the separate launches."""
         E, G, k, pe, l = self.num_experts, self.world, self.top_k, self.peer, self.layer_slot
         cap = pe.cap
+        partials = G * cap <= kernels.DECODE_MAX_ROWS
+        counters = None
         if h.shape[0] <= self._sms:
+            if partials:  # the front zeroes the expert stage's counters
+                if self._counters is None:
+                    self._counters = torch.zeros(kernels.expert_counter_words(self.inter),
+                                                 dtype=torch.int32, device=h.device)
+                counters = self._counters
             w, idx, slot_ep = kernels.ep_front_p2p(h, self.router.gate_f16(), k, E, G, self.rank,
                                                    cap, pe.peer_table(l, 0), pe.peer_table(l, 2),
-                                                   pe.seq(l, 0), pe.done(l, 0), pe.bar(l))
+                                                   pe.seq(l, 0), pe.done(l, 0), pe.bar(l),
+                                                   zero=counters)
         else:
             _, w, idx = kernels.router_topk(h, self.router.gate_f16(), k, with_logits=False)
             offsets, pair_token, _, pair_slot = kernels.permute(idx, w, E)
@@ -166,9 +175,9 @@ class ExpertParallelMoE:
                                               pe.peer_table(l, 2), pe.seq(l, 0), pe.done(l, 0))
         x_sorted, local_off, recv_counts = kernels.ep_receive_p2p(pe.recv_rows(l), E, G, cap,
                                                                   pe.own_flags(l, 0), pe.seq(l, 0))
-        if x_sorted.shape[0] <= kernels.DECODE_MAX_ROWS:
+        if partials:
             part = kernels.experts_forward_partials(self._table, local_off, x_sorted, self.hidden,
-                                                    self.inter)
+                                                    self.inter, counters=counters)
             kernels.ep_return_partials_p2p(part, recv_counts, E, G, self.rank, cap,
                                            pe.peer_table(l, 1), pe.peer_table(l, 3),
                                            pe.seq(l, 1), pe.done(l, 1))

@@ -8,6 +8,7 @@ with the library's status text on failure.  There is no CPU path.
 from __future__ import annotations
 
 import ctypes
+import functools
 from typing import Sequence
 
 import torch
@@ -25,6 +26,30 @@ def _p(t: torch.Tensor | None) -> ctypes.c_void_p | None:
 
 def _stream(device: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _on_device(fn):
+    """Run a wrapper with the device of its first CUDA tensor (or device) argument current.
+
+    The library launches on the stream it is given, and CUDA requires that stream to belong
+    to the current device (torch's default stream is the null handle: the current device's
+    own).  A call on another GPU's tensors than the current one switches devices for its
+    duration, and only then."""
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        dev = None
+        for a in (*args, *kwargs.values()):
+            if isinstance(a, torch.Tensor) and a.is_cuda:
+                dev = a.device.index
+                break
+            if isinstance(a, torch.device) and a.type == "cuda" and a.index is not None:
+                dev = a.index
+                break
+        if dev is None or dev == torch.cuda.current_device():
+            return fn(*args, **kwargs)
+        with torch.cuda.device(dev):
+            return fn(*args, **kwargs)
+    return wrapper
 
 
 def _need_cuda(what: str, **tensors: torch.Tensor) -> torch.device:
@@ -75,6 +100,7 @@ def check_device(device: torch.device | int | None = None) -> None:
         raise RuntimeError(f"device check failed: {_native.status_string(status)} (status {status})")
 
 
+@_on_device
 def probe_wait(flag: torch.Tensor, target: int = 1) -> torch.Tensor:
     """One bounded device wait until ``flag[0] >= target``; returns the device-side wait time (ns)."""
     dev = _need_cuda("probe_wait", flag=flag)
@@ -89,6 +115,7 @@ def probe_wait(flag: torch.Tensor, target: int = 1) -> torch.Tensor:
 # NF4 dequant
 # ---------------------------------------------------------------------------
 
+@_on_device
 def nf4_dequant(q: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, numel: int,
                 blocksize: int = NF4_BLOCKSIZE) -> torch.Tensor:
     """bf16 ``code[nib(i)] * absmax[i // blocksize]`` (bit-exact), flat [numel]."""
@@ -104,6 +131,7 @@ def nf4_dequant(q: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, numel
     return out
 
 
+@_on_device
 def nf4_tile16(q: torch.Tensor, absmax: torch.Tensor, rows: int, cols: int):
     """Store layout -> tile16 device layout (exact permutation); returns (q_t, absmax_t)."""
     dev = _need_cuda("nf4_tile16", q=q, absmax=absmax)
@@ -118,6 +146,7 @@ def nf4_tile16(q: torch.Tensor, absmax: torch.Tensor, rows: int, cols: int):
     return q_out, a_out
 
 
+@_on_device
 def nf4_dequant_tile16(q: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, rows: int,
                        cols: int) -> torch.Tensor:
     """bf16 [rows, cols] of a tile16 matrix (bit-exact with the store-layout dequant)."""
@@ -128,6 +157,7 @@ def nf4_dequant_tile16(q: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor
     return out
 
 
+@_on_device
 def nested_absmax(qabs: torch.Tensor, absmax2: torch.Tensor, code2: torch.Tensor,
                   offset: float, blocksize2: int = NESTED_BLOCKSIZE) -> torch.Tensor:
     dev = _need_cuda("nested_absmax", qabs=qabs, absmax2=absmax2, code2=code2)
@@ -148,6 +178,7 @@ def nested_absmax(qabs: torch.Tensor, absmax2: torch.Tensor, code2: torch.Tensor
 # Router
 # ---------------------------------------------------------------------------
 
+@_on_device
 def router_topk(h: torch.Tensor, wg: torch.Tensor, k: int, with_logits: bool = True):
     """``(logits fp16 [T,E] | None, weights fp32 [T,k], indices int64 [T,k])``."""
     dev = _need_cuda("router_topk", h=h, wg=wg)
@@ -163,6 +194,7 @@ def router_topk(h: torch.Tensor, wg: torch.Tensor, k: int, with_logits: bool = T
     return logits, w, idx
 
 
+@_on_device
 def router_topk_from_logits(logits: torch.Tensor, k: int):
     dev = _need_cuda("router_topk_from_logits", logits=logits)
     _need_dtype("router_topk_from_logits", logits, torch.float16, "logits")
@@ -182,6 +214,7 @@ def matrix_desc(q: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor) -> NF
     return NF4Matrix(q.data_ptr(), absmax.data_ptr(), code.data_ptr())
 
 
+@_on_device
 def expert_forward(desc: NF4Expert, x: torch.Tensor, hidden: int, inter: int) -> torch.Tensor:
     dev = _need_cuda("expert_forward", x=x)
     _need_dtype("expert_forward", x, torch.float16, "x")
@@ -224,6 +257,7 @@ def _layer_scratch(dev: torch.device, stream: int, T: int, hidden: int, inter: i
     return ent
 
 
+@_on_device
 def layer_forward(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hidden: int, inter: int,
                   out: torch.Tensor | None = None, routing: bool = True):
     """Fused MoE layer: returns ``(out fp16 [T,H], indices int64 [T,k], weights fp32 [T,k])``.
@@ -250,6 +284,7 @@ def layer_forward(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hidden: in
     return (out, idx, w) if routing else (out, None, None)
 
 
+@_on_device
 def layer_forward_noalloc(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hidden: int,
                           inter: int, out: torch.Tensor | None = None):
     """:func:`layer_forward` with the library's own static device scratch (no workspace).
@@ -273,6 +308,7 @@ def layer_forward_noalloc(h: torch.Tensor, wg: torch.Tensor, experts, k: int, hi
     return out, idx, w
 
 
+@_on_device
 def routed_layer_forward(h: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor, experts,
                          hidden: int, inter: int) -> torch.Tensor:
     """The MoE layer on routing the caller already has (indices int64 / weights fp32 [T, k]).
@@ -287,6 +323,7 @@ def routed_layer_forward(h: torch.Tensor, indices: torch.Tensor, weights: torch.
     return combine(y_sorted, pair_slot, indices.contiguous(), weights.contiguous())
 
 
+@_on_device
 def experts_forward(experts, expert_offsets: torch.Tensor, x_sorted: torch.Tensor, hidden: int,
                     inter: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """Expert stage on rows grouped by expert (``expert_offsets`` int32 [E+1] on device)."""
@@ -305,6 +342,7 @@ def experts_forward(experts, expert_offsets: torch.Tensor, x_sorted: torch.Tenso
     return out
 
 
+@_on_device
 def permute(indices: torch.Tensor, weights: torch.Tensor, num_experts: int):
     dev = _need_cuda("permute", indices=indices, weights=weights)
     _need_dtype("permute", indices, torch.int64, "indices")
@@ -321,6 +359,7 @@ def permute(indices: torch.Tensor, weights: torch.Tensor, num_experts: int):
     return offsets, pair_token, pair_weight, pair_slot
 
 
+@_on_device
 def gather_rows(rows: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
     dev = _need_cuda("gather_rows", rows=rows, index=index)
     _need_dtype("gather_rows", rows, torch.float16, "rows")
@@ -331,6 +370,7 @@ def gather_rows(rows: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
     return out
 
 
+@_on_device
 def combine(y_sorted: torch.Tensor, pair_slot: torch.Tensor, indices: torch.Tensor,
             weights: torch.Tensor) -> torch.Tensor:
     dev = _need_cuda("combine", y_sorted=y_sorted, pair_slot=pair_slot, indices=indices,
@@ -348,6 +388,7 @@ def combine(y_sorted: torch.Tensor, pair_slot: torch.Tensor, indices: torch.Tens
 # Expert-parallel exchange (pack / receive / return around two all-to-alls)
 # ---------------------------------------------------------------------------
 
+@_on_device
 def ep_dispatch(h: torch.Tensor, offsets: torch.Tensor, pair_token: torch.Tensor,
                 pair_slot: torch.Tensor, k: int, num_experts: int, world: int, cap: int):
     """``(send_rows fp16 [world*(cap+1), H], pair_slot_ep int32 [T*k])``.
@@ -366,6 +407,7 @@ def ep_dispatch(h: torch.Tensor, offsets: torch.Tensor, pair_token: torch.Tensor
     return send, slot_ep
 
 
+@_on_device
 def ep_receive(recv_rows: torch.Tensor, num_experts: int, world: int, cap: int):
     """``(x_sorted fp16 [world*cap, H], local_offsets int32 [E/world + 1], recv_counts int32 [E])``."""
     dev = _need_cuda("ep_receive", recv_rows=recv_rows)
@@ -378,6 +420,7 @@ def ep_receive(recv_rows: torch.Tensor, num_experts: int, world: int, cap: int):
     return x, off, counts
 
 
+@_on_device
 def ep_return(y_sorted: torch.Tensor, recv_counts: torch.Tensor, num_experts: int, world: int,
               cap: int) -> torch.Tensor:
     """``y_back fp16 [world*cap, H]`` in the exchanged (source rank, row) layout."""
@@ -393,6 +436,7 @@ def ep_return(y_sorted: torch.Tensor, recv_counts: torch.Tensor, num_experts: in
 # Expert-parallel exchange over peer memory (see moeinfra_b200.ep_p2p)
 # ---------------------------------------------------------------------------
 
+@_on_device
 def ep_dispatch_p2p(h: torch.Tensor, offsets: torch.Tensor, pair_token: torch.Tensor,
                     pair_slot: torch.Tensor, k: int, num_experts: int, world: int, rank: int,
                     cap: int, peer_recv: int, peer_flags: int, seq: int, done: int) -> torch.Tensor:
@@ -408,6 +452,7 @@ def ep_dispatch_p2p(h: torch.Tensor, offsets: torch.Tensor, pair_token: torch.Te
     return slot_ep
 
 
+@_on_device
 def ep_return_p2p(y_sorted: torch.Tensor, recv_counts: torch.Tensor, num_experts: int, world: int,
                   rank: int, cap: int, peer_back: int, peer_flags: int, seq: int, done: int) -> None:
     dev = _need_cuda("ep_return_p2p", y_sorted=y_sorted, recv_counts=recv_counts)
@@ -417,16 +462,19 @@ def ep_return_p2p(y_sorted: torch.Tensor, recv_counts: torch.Tensor, num_experts
                                           ctypes.c_void_p(done), _stream(dev)), "moe_ep_return_p2p")
 
 
+@_on_device
 def ep_wait_p2p(flags: int, world: int, seq: int, device: torch.device) -> None:
     check(_native.lib().moe_ep_wait_p2p(ctypes.c_void_p(flags), world, ctypes.c_void_p(seq),
                                         _stream(device)), "moe_ep_wait_p2p")
 
 
+@_on_device
 def ep_receive_rows(recv_rows: torch.Tensor, num_experts: int, world: int, cap: int):
     """:func:`ep_receive` on a receive region that is a view (peer-memory exchange)."""
     return ep_receive(recv_rows, num_experts, world, cap)
 
 
+@_on_device
 def ep_receive_p2p(recv_rows: torch.Tensor, num_experts: int, world: int, cap: int, flags: int,
                    seq: int):
     """:func:`ep_receive` of a peer-memory receive region, waiting (bounded, in the kernel)
@@ -443,6 +491,7 @@ def ep_receive_p2p(recv_rows: torch.Tensor, num_experts: int, world: int, cap: i
     return x, off, counts
 
 
+@_on_device
 def combine_p2p(y_back: torch.Tensor, pair_slot: torch.Tensor, indices: torch.Tensor,
                 weights: torch.Tensor, world: int, flags: int, seq: int) -> torch.Tensor:
     """:func:`combine` of a peer-memory return region, waiting (bounded, in the kernel) for all
@@ -459,13 +508,16 @@ def combine_p2p(y_back: torch.Tensor, pair_slot: torch.Tensor, indices: torch.Te
     return out
 
 
+@_on_device
 def ep_front_p2p(h: torch.Tensor, gate_f16: torch.Tensor, k: int, num_experts: int, world: int,
                  rank: int, cap: int, peer_recv: int, peer_flags: int, seq: int, done: int,
-                 bar: int):
+                 bar: int, zero: torch.Tensor | None = None):
     """Router, permute and the peer-memory dispatch in one launch (``T`` <= the SM count).
 
     Returns ``(weights fp32 [T, k], indices int64 [T, k], pair_slot_ep int32 [T*k])``, the
-    values :func:`router_topk`, :func:`permute` and :func:`ep_dispatch_p2p` give."""
+    values :func:`router_topk`, :func:`permute` and :func:`ep_dispatch_p2p` give.  ``zero``
+    (int32, optional) is zeroed by the same launch: the counters of the expert stage that
+    follows (:func:`experts_forward_partials` ``counters``)."""
     dev = _need_cuda("ep_front_p2p", h=h, gate_f16=gate_f16)
     _need_dtype("ep_front_p2p", h, torch.float16, "h")
     _need_dtype("ep_front_p2p", gate_f16, torch.float16, "gate_f16")
@@ -477,7 +529,10 @@ def ep_front_p2p(h: torch.Tensor, gate_f16: torch.Tensor, k: int, num_experts: i
                                          H, ctypes.c_void_p(peer_recv),
                                          ctypes.c_void_p(peer_flags), ctypes.c_void_p(seq),
                                          ctypes.c_void_p(done), ctypes.c_void_p(bar), _p(w),
-                                         _p(idx), _p(slot_ep), _stream(dev)), "moe_ep_front_p2p")
+                                         _p(idx), _p(slot_ep),
+                                         None if zero is None else _p(zero),
+                                         0 if zero is None else zero.numel(), _stream(dev)),
+          "moe_ep_front_p2p")
     return w, idx, slot_ep
 
 
@@ -486,10 +541,19 @@ def expert_splits(inter: int) -> int:
     return int(_native.lib().moe_expert_splits(inter))
 
 
+def expert_counter_words(inter: int) -> int:
+    """int32 completion counters of the decode expert stage (zeroed before each call)."""
+    return int(_native.lib().moe_experts_counter_words(inter))
+
+
+@_on_device
 def experts_forward_partials(experts, expert_offsets: torch.Tensor, x_sorted: torch.Tensor,
-                             hidden: int, inter: int) -> torch.Tensor:
+                             hidden: int, inter: int,
+                             counters: torch.Tensor | None = None) -> torch.Tensor:
     """:func:`experts_forward` of a decode batch (<= 8 rows) up to the down projection's
-    fp32 split partials ``[P, S, hidden]`` (their in-order fp16 sum is the output row)."""
+    fp32 split partials ``[P, S, hidden]`` (their in-order fp16 sum is the output row).
+    ``counters``: :func:`expert_counter_words` int32 already zeroed on the stream (by
+    :func:`ep_front_p2p`), which spares the zeroing launch; None zeroes internal ones."""
     dev = _need_cuda("experts_forward_partials", expert_offsets=expert_offsets, x_sorted=x_sorted)
     _need_dtype("experts_forward_partials", x_sorted, torch.float16, "x_sorted")
     _need_dtype("experts_forward_partials", expert_offsets, torch.int32, "expert_offsets")
@@ -498,13 +562,17 @@ def experts_forward_partials(experts, expert_offsets: torch.Tensor, x_sorted: to
     lib = _native.lib()
     ws_bytes = lib.moe_experts_workspace_size(P, hidden, inter)
     ws = _workspace(ws_bytes, dev)
+    if counters is not None and counters.numel() < expert_counter_words(inter):
+        raise ValueError("counters smaller than expert_counter_words(inter)")
     check(lib.moe_experts_forward_partials(experts, len(experts), _p(expert_offsets),
-                                           _p(x_sorted), P, hidden, inter, _p(part), _p(ws),
+                                           _p(x_sorted), P, hidden, inter, _p(part),
+                                           None if counters is None else _p(counters), _p(ws),
                                            ws_bytes, _stream(dev)),
           "moe_experts_forward_partials")
     return part
 
 
+@_on_device
 def ep_return_partials_p2p(y_part: torch.Tensor, recv_counts: torch.Tensor, num_experts: int,
                            world: int, rank: int, cap: int, peer_back: int, peer_flags: int,
                            seq: int, done: int) -> None:

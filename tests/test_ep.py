@@ -217,11 +217,15 @@ def test_ep_fused_p2p_kernels_emulated(G, T):
     t_back = table([b.data_ptr() for b in back])
     t_fd = table([f.data_ptr() for f in flags])
     t_fr = table([f.data_ptr() + 4 * G for f in flags])
+    # the expert-stage counters each rank's front zeroes (filled with junk first)
+    ctr = [torch.full((kernels.expert_counter_words(I),), 7, dtype=torch.int32, device=dev)
+           for _ in range(G)]
     front = []
     for s in range(G):
         wd = words[s].data_ptr()
         w, idx, slot_ep = kernels.ep_front_p2p(hs[s], wg, k, E, G, s, cap, t_recv.data_ptr(),
-                                               t_fd.data_ptr(), wd, wd + 8, wd + 16)
+                                               t_fd.data_ptr(), wd, wd + 8, wd + 16, zero=ctr[s])
+        assert int(ctr[s].abs().sum()) == 0
         # the separate launches it replaces
         _, w_ref, idx_ref = kernels.router_topk(hs[s], wg, k, with_logits=False)
         off, ptok, _, pslot = kernels.permute(idx_ref, w_ref, E)
@@ -248,7 +252,7 @@ def test_ep_fused_p2p_kernels_emulated(G, T):
         tab = kernels.expert_array([experts[e].nf4_descriptor for e in ep.local_experts(r, E, G)])
         y = kernels.experts_forward(tab, local_off, x, H, I)
         if G * cap <= kernels.DECODE_MAX_ROWS:
-            part = kernels.experts_forward_partials(tab, local_off, x, H, I)
+            part = kernels.experts_forward_partials(tab, local_off, x, H, I, counters=ctr[r])
             assert part.shape == (G * cap, kernels.expert_splits(I), H)
             kernels.ep_return_partials_p2p(part, counts, E, G, r, cap, t_back.data_ptr(),
                                            t_fr.data_ptr(), wd + 4, wd + 12)
