@@ -95,3 +95,34 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.delenv("MOE_B200_LIB")
     monkeypatch.setattr(_native, "_lib", None)
     _native.lib()
+
+
+def test_wrappers_make_their_tensors_device_current(monkeypatch):
+    """A call on another GPU's data runs with that GPU current (the library launches on the
+    current device); a call on the current GPU's data switches nothing.  Checked on the host
+    with the current device and the switch faked (no GPU needed)."""
+    import contextlib
+
+    import torch
+
+    from moeinfra_b200 import kernels
+
+    switched = []
+
+    @contextlib.contextmanager
+    def fake_device(d):
+        switched.append(d)
+        yield
+
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    monkeypatch.setattr(torch.cuda, "device", fake_device)
+
+    @kernels._on_device
+    def launch(n: int, device=None):
+        return n
+
+    assert launch(3, device=torch.device("cuda", 1)) == 3
+    assert switched == [1]
+    assert launch(4, device=torch.device("cuda", 0)) == 4
+    assert launch(5) == 5  # nothing on a GPU: no switch
+    assert switched == [1]
