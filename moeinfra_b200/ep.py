@@ -153,8 +153,8 @@ class ExpertParallelMoE:
         dispatch in one kernel); a receive of at most ``DECODE_MAX_ROWS`` rows hands the expert
         stage's fp32 split partials to the return kernel, which sums them on the way out.  Both
         give the bits of the separate launches."""
-        E, G, k, pe, l = self.num_experts, self.world, self.top_k, self.peer, self.layer_slot
-        cap = pe.cap
+        E, G, k, cap = self.num_experts, self.world, self.top_k, self.peer.cap
+        R = self.peer.layer(self.layer_slot)
         partials = G * cap <= kernels.DECODE_MAX_ROWS
         counters = None
         if h.shape[0] <= self._sms:
@@ -164,29 +164,25 @@ class ExpertParallelMoE:
                                                  dtype=torch.int32, device=h.device)
                 counters = self._counters
             w, idx, slot_ep = kernels.ep_front_p2p(h, self.router.gate_f16(), k, E, G, self.rank,
-                                                   cap, pe.peer_table(l, 0), pe.peer_table(l, 2),
-                                                   pe.seq(l, 0), pe.done(l, 0), pe.bar(l),
-                                                   zero=counters)
+                                                   cap, R.recv_table, R.dflag_table, R.seq_d,
+                                                   R.done_d, R.bar, zero=counters)
         else:
             _, w, idx = kernels.router_topk(h, self.router.gate_f16(), k, with_logits=False)
             offsets, pair_token, _, pair_slot = kernels.permute(idx, w, E)
             slot_ep = kernels.ep_dispatch_p2p(h, offsets, pair_token, pair_slot, k, E, G,
-                                              self.rank, cap, pe.peer_table(l, 0),
-                                              pe.peer_table(l, 2), pe.seq(l, 0), pe.done(l, 0))
-        x_sorted, local_off, recv_counts = kernels.ep_receive_p2p(pe.recv_rows(l), E, G, cap,
-                                                                  pe.own_flags(l, 0), pe.seq(l, 0))
+                                              self.rank, cap, R.recv_table, R.dflag_table,
+                                              R.seq_d, R.done_d)
+        x_sorted, local_off, recv_counts = kernels.ep_receive_p2p(R.recv, E, G, cap, R.dflags,
+                                                                  R.seq_d)
         if partials:
             part = kernels.experts_forward_partials(self._table, local_off, x_sorted, self.hidden,
                                                     self.inter, counters=counters)
-            kernels.ep_return_partials_p2p(part, recv_counts, E, G, self.rank, cap,
-                                           pe.peer_table(l, 1), pe.peer_table(l, 3),
-                                           pe.seq(l, 1), pe.done(l, 1))
+            kernels.ep_return_partials_p2p(part, recv_counts, E, G, self.rank, cap, R.back_table,
+                                           R.rflag_table, R.seq_r, R.done_r)
         else:
             y_sorted = kernels.experts_forward(self._table, local_off, x_sorted, self.hidden,
                                                self.inter)
-            kernels.ep_return_p2p(y_sorted, recv_counts, E, G, self.rank, cap,
-                                  pe.peer_table(l, 1), pe.peer_table(l, 3), pe.seq(l, 1),
-                                  pe.done(l, 1))
-        return kernels.combine_p2p(pe.back_rows(l), slot_ep, idx, w, G, pe.own_flags(l, 1),
-                                   pe.seq(l, 1))
+            kernels.ep_return_p2p(y_sorted, recv_counts, E, G, self.rank, cap, R.back_table,
+                                  R.rflag_table, R.seq_r, R.done_r)
+        return kernels.combine_p2p(R.back, slot_ep, idx, w, G, R.rflags, R.seq_r)
 

@@ -27,6 +27,8 @@ of the same region, and every layer's exchanges order the ranks.
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 import torch.distributed as dist
 
@@ -45,6 +47,24 @@ def _check(ret, what: str):
     if not isinstance(ret, tuple) or len(ret) == 1:
         return None
     return ret[1] if len(ret) == 2 else ret[1:]
+
+
+@dataclass(frozen=True)
+class LayerRegions:
+    """Every address one layer's two exchanges use (device addresses as ints)."""
+    recv_table: int   # [G] uint64: each rank's receive region
+    back_table: int   # [G] uint64: each rank's return region
+    dflag_table: int  # [G] uint64: each rank's dispatch flags
+    rflag_table: int  # [G] uint64: each rank's return flags
+    recv: torch.Tensor  # this rank's receive region, fp16 rows [G*(cap+1), hidden]
+    back: torch.Tensor  # this rank's return region, fp16 rows [G*cap, hidden]
+    dflags: int
+    rflags: int
+    seq_d: int
+    seq_r: int
+    done_d: int
+    done_r: int
+    bar: int
 
 
 class PeerExchange:
@@ -96,6 +116,7 @@ class PeerExchange:
                          [a + lo + self.recv_bytes + self.back_bytes + 4 * G for a in addrs]])
         # device tables [layers, 4, G] of uint64 addresses
         self.tables = torch.tensor(tabs, dtype=torch.int64, device=self.device)
+        self._layers: dict = {}
         torch.distributed.barrier(group=group)
 
     # -- per-layer addresses -------------------------------------------------------------
@@ -132,6 +153,18 @@ class PeerExchange:
     def bar(self, l: int) -> int:
         """The grid-barrier words (arrivals, generation) of layer ``l``'s front launch."""
         return self.seq(l, 0) + 16
+
+    def layer(self, l: int) -> LayerRegions:
+        """Layer ``l``'s addresses, computed once (the regions never move), so that a call
+        on the host does no tensor indexing to find them."""
+        got = self._layers.get(l)
+        if got is None:
+            got = LayerRegions(self.peer_table(l, 0), self.peer_table(l, 1), self.peer_table(l, 2),
+                               self.peer_table(l, 3), self.recv_rows(l), self.back_rows(l),
+                               self.own_flags(l, 0), self.own_flags(l, 1), self.seq(l, 0),
+                               self.seq(l, 1), self.done(l, 0), self.done(l, 1), self.bar(l))
+            self._layers[l] = got
+        return got
 
     def close(self) -> None:
         from cuda.bindings import runtime as rt

@@ -75,6 +75,38 @@ def test_sharding_helpers():
         ep.check_layout(8, 3)
 
 
+def test_peer_layer_regions_match_the_address_methods():
+    """The per-layer address record the layer uses is exactly the address methods' values
+    (checked on host tensors: the arithmetic needs no GPU), and it is computed once."""
+    from moeinfra_b200.ep_p2p import PeerExchange, _align
+
+    pe = object.__new__(PeerExchange)
+    pe.layers, pe.world, pe.rank, pe.cap, pe.hidden = 3, 4, 1, 2, 64
+    G = pe.world
+    pe.recv_bytes = _align(G * (pe.cap + 1) * pe.hidden * 2)
+    pe.back_bytes = _align(G * pe.cap * pe.hidden * 2)
+    pe.flag_bytes = _align(2 * G * 4)
+    pe.local_bytes = _align(6 * 4)
+    pe.layer_bytes = pe.recv_bytes + pe.back_bytes + pe.flag_bytes + pe.local_bytes
+    pe.buf = torch.zeros(pe.layer_bytes * pe.layers, dtype=torch.uint8)
+    pe.tables = torch.arange(pe.layers * 4 * G, dtype=torch.int64).view(pe.layers, 4, G)
+    pe._layers = {}
+    for l in range(pe.layers):
+        R = pe.layer(l)
+        assert [R.recv_table, R.back_table, R.dflag_table, R.rflag_table] == \
+            [pe.peer_table(l, w) for w in range(4)]
+        assert (R.dflags, R.rflags, R.seq_d, R.seq_r, R.done_d, R.done_r, R.bar) == \
+            (pe.own_flags(l, 0), pe.own_flags(l, 1), pe.seq(l, 0), pe.seq(l, 1), pe.done(l, 0),
+             pe.done(l, 1), pe.bar(l))
+        assert R.recv.data_ptr() == pe.recv_rows(l).data_ptr()
+        assert R.recv.shape == (G * (pe.cap + 1), pe.hidden)
+        assert R.back.data_ptr() == pe.back_rows(l).data_ptr()
+        assert R.back.shape == (G * pe.cap, pe.hidden)
+        assert pe.layer(l) is R
+    # the words of one layer do not overlap the next layer's regions
+    assert pe.layer(0).bar + 8 <= pe.buf.data_ptr() + pe.layer_bytes
+
+
 def _a2a(out: torch.Tensor, inp: torch.Tensor):
     """all_to_all_single on fp16 rows through an int32 view (gloo has no fp16 all-to-all)."""
     if inp.dtype == torch.float16:
