@@ -107,6 +107,89 @@ def test_peer_layer_regions_match_the_address_methods():
     assert pe.layer(0).bar + 8 <= pe.buf.data_ptr() + pe.layer_bytes
 
 
+def _fake_peer(world: int, cap: int, hidden: int, layers: int):
+    from moeinfra_b200.ep_p2p import PeerExchange, _align
+
+    pe = object.__new__(PeerExchange)
+    pe.layers, pe.world, pe.rank, pe.cap, pe.hidden = layers, world, 0, cap, hidden
+    pe.recv_bytes = _align(world * (cap + 1) * hidden * 2)
+    pe.back_bytes = _align(world * cap * hidden * 2)
+    pe.flag_bytes = _align(2 * world * 4)
+    pe.local_bytes = _align(6 * 4)
+    pe.layer_bytes = pe.recv_bytes + pe.back_bytes + pe.flag_bytes + pe.local_bytes
+    pe.buf = torch.zeros(pe.layer_bytes * layers, dtype=torch.uint8)
+    pe.tables = torch.arange(layers * 4 * world, dtype=torch.int64).view(layers, 4, world) + 1000
+    pe._layers = {}
+    return pe
+
+
+@pytest.mark.parametrize("world,T", [(2, 1), (8, 1), (2, 3)])
+def test_peer_layer_passes_each_kernel_its_regions(monkeypatch, world, T):
+    """The peer-memory layer's launches get this layer's addresses, in the roles the C ABI
+    gives them (recorded on the host with the kernels replaced by recorders)."""
+    from moeinfra_b200 import kernels
+
+    E, k, H, I, l = 8, 2, 64, 128, 1
+    cap = ep.capacity(T, k, E, world)
+    pe = _fake_peer(world, cap, H, layers=2)
+    calls = {}
+
+    def rec(name, ret=None):
+        def f(*args, **kw):
+            calls[name] = (args, kw)
+            return ret() if ret else None
+        return f
+
+    P = world * cap
+    monkeypatch.setattr(kernels, "ep_front_p2p", rec("front", lambda: (
+        torch.zeros(T, k), torch.zeros(T, k, dtype=torch.int64), torch.zeros(T * k))))
+    monkeypatch.setattr(kernels, "ep_receive_p2p", rec("receive", lambda: (
+        torch.zeros(P, H), torch.zeros(E // world + 1), torch.zeros(E))))
+    monkeypatch.setattr(kernels, "experts_forward_partials", rec("stage_part", lambda: "part"))
+    monkeypatch.setattr(kernels, "experts_forward", rec("stage", lambda: "y"))
+    monkeypatch.setattr(kernels, "ep_return_partials_p2p", rec("return_part"))
+    monkeypatch.setattr(kernels, "ep_return_p2p", rec("return"))
+    monkeypatch.setattr(kernels, "combine_p2p", rec("combine", lambda: "out"))
+    monkeypatch.setattr(kernels, "expert_counter_words", lambda inter: 16)
+
+    class Router:
+        num_experts, num_experts_per_tok = E, k
+
+        def gate_f16(self):
+            return torch.zeros(E, H)
+
+    layer = object.__new__(ep.ExpertParallelMoE)
+    layer.router, layer.num_experts, layer.top_k = Router(), E, k
+    layer.rank, layer.world, layer.group = 0, world, None
+    layer.max_tokens, layer.cap, layer.hidden, layer.inter = T, cap, H, I
+    layer._table, layer.peer, layer.layer_slot = "table", pe, l
+    layer._sms, layer._counters = 148, None
+    assert layer._forward_p2p(torch.zeros(T, H)) == "out"
+
+    R = pe.layer(l)
+    args, kw = calls["front"]
+    assert args[7:12] == (pe.peer_table(l, 0), pe.peer_table(l, 2), pe.seq(l, 0), pe.done(l, 0),
+                          pe.bar(l))
+    args, _ = calls["receive"]
+    assert args[0].data_ptr() == pe.recv_rows(l).data_ptr()
+    assert args[4:6] == (pe.own_flags(l, 0), pe.seq(l, 0))
+    partials = P <= kernels.DECODE_MAX_ROWS
+    if partials:
+        assert kw["zero"] is layer._counters
+        assert calls["stage_part"][1]["counters"] is layer._counters
+        args, _ = calls["return_part"]
+        assert "stage" not in calls and "return" not in calls
+    else:
+        assert kw["zero"] is None
+        args, _ = calls["return"]
+        assert "stage_part" not in calls and "return_part" not in calls
+    assert args[6:10] == (pe.peer_table(l, 1), pe.peer_table(l, 3), pe.seq(l, 1), pe.done(l, 1))
+    args, _ = calls["combine"]
+    assert args[0].data_ptr() == pe.back_rows(l).data_ptr()
+    assert args[5:7] == (pe.own_flags(l, 1), pe.seq(l, 1))
+    assert R.back.data_ptr() == pe.back_rows(l).data_ptr()
+
+
 def _a2a(out: torch.Tensor, inp: torch.Tensor):
     """all_to_all_single on fp16 rows through an int32 view (gloo has no fp16 all-to-all)."""
     if inp.dtype == torch.float16:
