@@ -107,6 +107,47 @@ def test_peer_layer_regions_match_the_address_methods():
     assert pe.layer(0).bar + 8 <= pe.buf.data_ptr() + pe.layer_bytes
 
 
+def _front_placement(h: torch.Tensor, idx: torch.Tensor, E: int, G: int, cap: int):
+    """The fused front kernel's placement rule, restated on the host: each token, knowing
+    only every token's experts, puts pair (t, j) at s_off[e] + (pairs of e before token t)
+    and its row there in owner e // El's chunk."""
+    T, k = idx.shape
+    El = E // G
+    flat = idx.reshape(-1)
+    total = torch.bincount(flat, minlength=E)
+    s_off = torch.zeros(E + 1, dtype=torch.int64)
+    s_off[1:] = torch.cumsum(total, 0)
+    send = torch.zeros(G * (cap + 1), h.shape[1], dtype=h.dtype)
+    slot_ep = torch.empty(T * k, dtype=torch.int32)
+    for t in range(T):
+        before = torch.bincount(flat[:t * k], minlength=E)
+        for j in range(k):
+            e = int(idx[t, j])
+            r = e // El
+            i = int(s_off[e] + before[e] - s_off[r * El])
+            slot_ep[t * k + j] = r * cap + i
+            send[r * (cap + 1) + i] = h[t]
+    for r in range(G):
+        send[r * (cap + 1) + cap].view(torch.int32)[:El] = total[r * El:(r + 1) * El].to(torch.int32)
+    return send, slot_ep
+
+
+@pytest.mark.parametrize("E,G,k,T", [(8, 8, 2, 1), (8, 8, 2, 148), (8, 4, 2, 37), (8, 2, 8, 5),
+                                     (16, 4, 4, 64), (16, 16, 1, 100), (32, 8, 8, 148)])
+def test_front_placement_rule_equals_permute_then_dispatch(E, G, k, T):
+    """The fused front's order (counting earlier tokens' pairs per expert) is exactly the
+    stable sort of moe_permute followed by the dispatch, for any routing of distinct experts
+    per token, up to one token per SM."""
+    g = torch.Generator().manual_seed(E * 1000 + G * 100 + k * 10 + T)
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    h = torch.randn(T, 16, generator=g).half()
+    cap = ep.capacity(T, k, E, G)
+    want_send, _, want_slot = oep.dispatch(h, idx, E, G, cap)
+    got_send, got_slot = _front_placement(h, idx, E, G, cap)
+    assert torch.equal(got_slot, want_slot)
+    assert torch.equal(got_send.view(torch.int16), want_send.view(torch.int16))
+
+
 def _fake_peer(world: int, cap: int, hidden: int, layers: int):
     from moeinfra_b200.ep_p2p import PeerExchange, _align
 
