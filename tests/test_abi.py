@@ -126,3 +126,30 @@ def test_wrappers_make_their_tensors_device_current(monkeypatch):
     assert launch(4, device=torch.device("cuda", 0)) == 4
     assert launch(5) == 5  # nothing on a GPU: no switch
     assert switched == [1]
+
+
+def test_fused_exchange_entries_check_arguments_before_any_launch():
+    """The fused expert-parallel entry points refuse bad calls on the host (no pointer below is
+    dereferenced: every check precedes the launch)."""
+    lib = _native.lib()
+    f = ctypes.c_void_p(0x100000)  # 16-byte aligned, never read
+
+    def front(T, E, k, G, rank, cap, hidden=4096, n_zero=0):
+        return lib.moe_ep_front_p2p(f, f, T, E, k, G, rank, cap, hidden, f, f, f, f, f, f, f, f,
+                                    f, n_zero, None)
+
+    assert front(1, 8, 9, 8, 0, 1) == 1        # k > 8
+    assert front(1, 8, 2, 8, 8, 1) == 1        # rank outside [0, G)
+    assert front(2, 8, 2, 8, 0, 1) == 1        # T * min(k, E/G) rows exceed cap
+    assert front(1, 8, 2, 3, 0, 2) == 1        # E not a multiple of G
+    assert front(1, 8, 2, 8, 0, 1, n_zero=-1) == 1
+    assert front(149, 8, 2, 8, 0, 149) == 2    # more tokens than SMs: CTAs not all resident
+    assert lib.moe_ep_front_p2p(None, None, 1, 8, 2, 8, 0, 1, 4096, f, f, f, f, None, f, f, f,
+                                None, 0, None) == 1  # no barrier words
+    # partials: decode-sized calls only; the return needs S >= 1
+    desc = (_native.NF4Expert * 1)()
+    assert lib.moe_experts_forward_partials(desc, 1, f, f, 9, 4096, 14336, f, None, f, 1 << 30,
+                                            None) == 2
+    assert lib.moe_ep_return_partials_p2p(f, 0, f, 8, 8, 0, 1, 4096, f, f, f, f, None) == 1
+    assert lib.moe_expert_splits(14336) == 7 and lib.moe_expert_splits(100) == -1
+    assert lib.moe_experts_counter_words(14336) == 2 * 16 * 7
